@@ -1,0 +1,926 @@
+// ljx engine: the extern "C" layer of include/ljx.h. Replaces the reference's PJRT runtime
+// (cpp/pjrt/runtime.{h,cpp}) and the Kokkos pack/add/virial/comm functors of
+// cpp/pair_jax_kokkos.cpp with hand-written sm_100a kernels (kernels.cuh). Buffers are sized
+// once from the bundle contract; no call allocates or synchronizes except ljx_read_result.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "bundle.h"
+#include "kernels.cuh"
+#include "ljx.h"
+
+#define LJX_VERSION "0.1.0"
+
+namespace {
+
+thread_local std::string g_bundle_error;
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+void check(cudaError_t err, const char *what)
+{
+  if (err != cudaSuccess)
+    throw CudaError(std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+template <typename Kernel>
+int blocks_per_sm(Kernel kernel)
+{
+  static std::unordered_map<const void *, int> cache;
+  const void *key = reinterpret_cast<const void *>(kernel);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, ljx::kBlock, 0),
+        "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  n = std::max(1, std::min(n, 8));
+  cache.emplace(key, n);
+  return n;
+}
+
+}  // namespace
+
+struct ljx_bundle {
+  ljx::Bundle b;
+};
+
+struct ljx_engine {
+  ljx::Bundle bundle;
+  ljx_contract c{};
+  int device = 0;
+  int sm_count = 148;
+  bool f64 = true;
+  int rows_cap = 0;     // list rows the compacted buffer holds
+  int row_cap = 0;      // kept pairs per compacted row
+  int max_grid = 0;     // partial rows per kernel kind
+  // Device buffers.
+  double4 *xd4 = nullptr;
+  void *pos4 = nullptr;
+  void *rho = nullptr;
+  void *fp = nullptr;
+  int *cedges = nullptr;
+  int *ccount = nullptr;
+  void *embedding = nullptr;
+  void *density = nullptr;
+  void *pair = nullptr;
+  int *senders = nullptr;
+  int *receivers = nullptr;
+  uint8_t *edge_mask = nullptr;
+  long long *offsets = nullptr;
+  long long *count_prev = nullptr;
+  double *partials = nullptr;   // [4][max_grid][kPartialWidth]: density, embed, force, lj
+  double *result = nullptr;     // [9]
+  double *host_result = nullptr;
+  // Step state: partial rows written by this step's kernels.
+  int step_blocks[4] = {0, 0, 0, 0};
+  int last_nlocal = 0;
+  int last_nall = 0;
+  double last_scale = 1.0;
+  int last_duplicate = 1;
+  long long launches = 0;
+  std::string error;
+
+  ~ljx_engine()
+  {
+    cudaSetDevice(device);
+    void *ptrs[] = {xd4,     pos4,      rho,       fp,      cedges,     ccount,
+                    embedding, density, pair,      senders, receivers,  edge_mask,
+                    offsets, count_prev, partials, result};
+    for (void *p : ptrs)
+      if (p) cudaFree(p);
+    if (host_result) cudaFreeHost(host_result);
+  }
+
+  double *partial(int kind) const
+  {
+    return partials + static_cast<long long>(kind) * max_grid * ljx::kPartialWidth;
+  }
+};
+
+namespace {
+
+enum PartialKind { kDensityPart = 0, kEmbedPart = 1, kForcePart = 2, kLjPart = 3 };
+
+struct DeviceGuard {
+  int previous = -1;
+  explicit DeviceGuard(int device)
+  {
+    check(cudaGetDevice(&previous), "cudaGetDevice");
+    if (previous != device) check(cudaSetDevice(device), "cudaSetDevice");
+  }
+  ~DeviceGuard()
+  {
+    int now = -1;
+    if (cudaGetDevice(&now) == cudaSuccess && now != previous && previous >= 0)
+      cudaSetDevice(previous);
+  }
+};
+
+template <typename F>
+ljx_status guarded(ljx_engine *e, F &&body)
+{
+  if (e == nullptr) return LJX_ERR_INVALID;
+  try {
+    DeviceGuard guard(e->device);
+    return body();
+  } catch (const CudaError &err) {
+    e->error = err.what();
+    return LJX_ERR_CUDA;
+  } catch (const std::exception &err) {
+    e->error = err.what();
+    return LJX_ERR_INVALID;
+  }
+}
+
+ljx_status fail(ljx_engine *e, ljx_status status, const std::string &message)
+{
+  e->error = message;
+  return status;
+}
+
+void *device_alloc(size_t bytes, const char *what)
+{
+  void *p = nullptr;
+  if (bytes == 0) bytes = 16;
+  check(cudaMalloc(&p, bytes), what);
+  return p;
+}
+
+template <typename T>
+void *upload_table(const std::vector<double> &values)
+{
+  std::vector<T> cast(values.begin(), values.end());
+  void *p = device_alloc(cast.size() * sizeof(T), "cudaMalloc(table)");
+  check(cudaMemcpy(p, cast.data(), cast.size() * sizeof(T), cudaMemcpyHostToDevice),
+        "cudaMemcpy(table)");
+  return p;
+}
+
+// Force distribution and list kind, decided as PairJaxKokkos::half_list / compute do.
+struct Modes {
+  bool half_list = false;
+  int density = ljx::kDensityFull;
+  int force = ljx::kRowsFull;
+  int lj = ljx::kLjEdgeFull;
+  bool forward_fp = false;
+  bool reverse_density = false;
+  bool reverse_force = false;
+  bool duplicate = false;
+};
+
+Modes decide_modes(const ljx_contract &c, int newton_pair)
+{
+  Modes m;
+  const bool comm = c.n_comm_widths > 0;
+  const bool matrix = c.input_layout == LJX_LAYOUT_NEIGHBOR_MATRIX;
+  const bool edge_force = c.force_layout == LJX_FORCE_EDGE;
+  // cpp/pair_jax_kokkos.cpp:425-431.
+  if (!newton_pair)
+    m.half_list = false;
+  else if (comm)
+    m.half_list = c.half_edges != 0;
+  else if (matrix)
+    m.half_list = false;
+  else
+    m.half_list = c.n_hops == 1 && (edge_force || c.pair_sum);
+  m.duplicate = newton_pair && c.pair_sum && !edge_force && c.n_hops == 1 && !comm;
+  if (c.potential == LJX_POTENTIAL_EAM) {
+    if (m.half_list) {
+      m.density = ljx::kDensityHalf;
+      m.force = ljx::kHalf;
+      m.reverse_density = true;
+      m.forward_fp = true;
+      m.reverse_force = true;
+    } else if (newton_pair) {
+      m.force = ljx::kGhost;
+      m.reverse_force = true;
+    } else {
+      m.force = ljx::kRowsFull;
+      m.forward_fp = true;
+    }
+  } else if (c.potential == LJX_POTENTIAL_LJ) {
+    if (edge_force)
+      m.lj = m.half_list ? ljx::kLjEdgeHalf : ljx::kLjEdgeFull;
+    else
+      m.lj = m.half_list ? ljx::kLjAtomHalfPairSum : ljx::kLjAtomFull;
+    m.reverse_force = newton_pair != 0;
+  }
+  return m;
+}
+
+template <typename T>
+ljx::Step<T> make_step(ljx_engine *e, const ljx_atoms *a, const ljx_list *l, double scale)
+{
+  using V = typename ljx::Vec4<T>::type;
+  ljx::Step<T> p{};
+  if (a) {
+    p.x = a->x;
+    p.type = a->type;
+    p.f = a->f;
+    p.nlocal = a->nlocal;
+    p.nghost = a->nghost;
+    p.nall = a->nlocal + a->nghost;
+  }
+  if (l) {
+    p.ilist = l->ilist;
+    p.numneigh = l->numneigh;
+    p.neighbors = l->neighbors;
+    p.atom_stride = l->atom_stride;
+    p.slot_stride = l->slot_stride;
+    p.inum = l->inum;
+    p.maxneighs = std::max(1, l->maxneighs);
+  }
+  p.xd4 = e->xd4;
+  p.pos4 = static_cast<V *>(e->pos4);
+  p.rho = static_cast<T *>(e->rho);
+  p.fp = static_cast<T *>(e->fp);
+  p.cedges = e->cedges;
+  p.ccount = e->ccount;
+  p.row_cap = e->row_cap;
+  p.embedding = static_cast<const V *>(e->embedding);
+  p.density = static_cast<const V *>(e->density);
+  p.pair = static_cast<const V *>(e->pair);
+  p.nrho = e->bundle.eam.nrho;
+  p.nr = e->bundle.eam.nr;
+  p.drho = static_cast<T>(e->bundle.eam.drho);
+  p.inv_dr = e->bundle.eam.dr > 0 ? static_cast<T>(1.0 / e->bundle.eam.dr) : T(0);
+  p.pack_cutsq = e->c.cutoff * e->c.cutoff;
+  const double model_cut =
+      e->c.potential == LJX_POTENTIAL_EAM ? e->bundle.eam.cutoff : e->c.cutoff;
+  p.model_cutsq = static_cast<T>(model_cut * model_cut);
+  p.max_atoms = e->c.max_atoms;
+  p.scale = scale;
+  p.lj_four_eps = static_cast<T>(4.0 * e->c.lj_epsilon);
+  p.lj_sigma_sq = static_cast<T>(e->c.lj_sigma * e->c.lj_sigma);
+  p.lj_energy_scale = static_cast<T>(e->c.lj_edge_energy_scale);
+  return p;
+}
+
+// Packer rules of cpp/pair_jax_kokkos.cpp:853-865 for the list the run hands over.
+template <typename T>
+void set_pack_rules(ljx::Step<T> &p, const ljx_contract &c, const Modes &m)
+{
+  const bool full_list = !m.half_list;
+  p.half_rule = c.half_edges && full_list;
+  p.unique_rule = c.half_edges && c.n_comm_widths > 0 && full_list;
+}
+
+int row_grid(ljx_engine *e, int rows, int per_sm)
+{
+  const int need = (rows + ljx::kWarpsPerBlock - 1) / ljx::kWarpsPerBlock;
+  return std::max(1, std::min(need, std::min(e->max_grid, e->sm_count * per_sm)));
+}
+
+int flat_grid(long long items)
+{
+  const long long need = (items + ljx::kBlock - 1) / ljx::kBlock;
+  return static_cast<int>(std::max<long long>(1, std::min<long long>(need, 148LL * 16)));
+}
+
+void check_launch(const char *what) { check(cudaGetLastError(), what); }
+
+ljx_status check_capacity(ljx_engine *e, const ljx_atoms *a)
+{
+  // Pre-launch row limits, cpp/pair_jax_kokkos.cpp:1035-1046 (rank-local values; the pair
+  // style takes the global max first).
+  const int nall = a->nlocal + a->nghost;
+  if (nall > e->c.max_atoms)
+    return fail(e, LJX_ERR_CAPACITY,
+                "LAMMPS-JAX atom capacity exceeded: global max " + std::to_string(nall) +
+                    " atoms, capacity " + std::to_string(e->c.max_atoms));
+  if (e->c.max_owned > 0 && a->nlocal > e->c.max_owned)
+    return fail(e, LJX_ERR_CAPACITY,
+                "LAMMPS-JAX owned-row capacity exceeded: global max " +
+                    std::to_string(a->nlocal) + " owned atoms, capacity " +
+                    std::to_string(e->c.max_owned));
+  return LJX_OK;
+}
+
+ljx_status check_list(ljx_engine *e, const ljx_list *l)
+{
+  if (l == nullptr || (l->inum > 0 && (!l->ilist || !l->numneigh || !l->neighbors)))
+    return fail(e, LJX_ERR_INVALID, "neighbor list view is incomplete");
+  if (l->inum > e->rows_cap)
+    return fail(e, LJX_ERR_CAPACITY,
+                "LAMMPS-JAX owned-row capacity exceeded: global max " + std::to_string(l->inum) +
+                    " list rows, capacity " + std::to_string(e->rows_cap));
+  if (l->gnum > 0)
+    return fail(e, LJX_ERR_UNSUPPORTED, "ljx runs single-hop bundles; ghost list rows are unused");
+  return LJX_OK;
+}
+
+template <typename T>
+void launch_density(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+{
+  if (p.inum <= 0) return;
+  int grid = 0;
+  switch (mode) {
+    case ljx::kDensityHalf:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_density<T, ljx::kDensityHalf>));
+      ljx::k_density<T, ljx::kDensityHalf><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
+    case ljx::kCompactOnly:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_density<T, ljx::kCompactOnly>));
+      ljx::k_density<T, ljx::kCompactOnly><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
+    default:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_density<T, ljx::kDensityFull>));
+      ljx::k_density<T, ljx::kDensityFull><<<grid, ljx::kBlock, 0, s>>>(p);
+  }
+  check_launch("k_density");
+  e->launches++;
+  e->step_blocks[kDensityPart] = grid;
+}
+
+template <typename T>
+void launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+{
+  if (p.inum <= 0) return;
+  int grid = 0;
+  switch (mode) {
+    case ljx::kGhost:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kGhost>));
+      ljx::k_force<T, ljx::kGhost><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
+    case ljx::kHalf:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kHalf>));
+      ljx::k_force<T, ljx::kHalf><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
+    default:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kRowsFull>));
+      ljx::k_force<T, ljx::kRowsFull><<<grid, ljx::kBlock, 0, s>>>(p);
+  }
+  check_launch("k_force");
+  e->launches++;
+  e->step_blocks[kForcePart] = grid;
+}
+
+template <typename T>
+void launch_lj(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+{
+  if (p.inum <= 0) return;
+  int grid = 0;
+  switch (mode) {
+    case ljx::kLjEdgeHalf:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeHalf>));
+      ljx::k_lj<T, ljx::kLjEdgeHalf><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
+    case ljx::kLjAtomFull:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomFull>));
+      ljx::k_lj<T, ljx::kLjAtomFull><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
+    case ljx::kLjAtomHalfPairSum:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomHalfPairSum>));
+      ljx::k_lj<T, ljx::kLjAtomHalfPairSum><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
+    default:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeFull>));
+      ljx::k_lj<T, ljx::kLjEdgeFull><<<grid, ljx::kBlock, 0, s>>>(p);
+  }
+  check_launch("k_lj");
+  e->launches++;
+  e->step_blocks[kLjPart] = grid;
+}
+
+template <typename T>
+ljx_status pack_edges_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
+                           int newton_pair)
+{
+  const Modes m = decide_modes(e->c, newton_pair);
+  ljx::Step<T> p = make_step<T>(e, a, l, 1.0);
+  set_pack_rules(p, e->c, m);
+  p.partials = e->partial(kDensityPart);
+  launch_density<T>(e, s, p, ljx::kCompactOnly);
+  const int rows = std::max(0, p.inum);
+  ljx::k_scan_counts<<<1, 1024, 0, s>>>(e->ccount, rows, m.duplicate ? 2 : 1, e->offsets);
+  check_launch("k_scan_counts");
+  e->launches++;
+  if (rows > 0) {
+    const int grid = row_grid(e, rows, blocks_per_sm(ljx::k_emit_edges<T>));
+    ljx::k_emit_edges<T><<<grid, ljx::kBlock, 0, s>>>(p, e->offsets, m.duplicate ? 1 : 0,
+                                                       e->c.max_edges, e->senders, e->receivers,
+                                                       e->edge_mask);
+    check_launch("k_emit_edges");
+    e->launches++;
+  }
+  ljx::k_reset_tail<<<e->sm_count * 4, ljx::kBlock, 0, s>>>(e->offsets + rows, e->count_prev,
+                                                            e->c.max_atoms, e->c.max_edges,
+                                                            e->senders, e->receivers, e->edge_mask);
+  check_launch("k_reset_tail");
+  ljx::k_store_prev<<<1, 1, 0, s>>>(e->offsets + rows, e->count_prev);
+  check_launch("k_store_prev");
+  e->launches += 2;
+  e->last_duplicate = m.duplicate ? 2 : 1;
+  return LJX_OK;
+}
+
+template <typename T>
+ljx_status density_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
+                        int newton_pair)
+{
+  const Modes m = decide_modes(e->c, newton_pair);
+  if (e->c.potential == LJX_POTENTIAL_LJ) return LJX_OK;  // LJ is one pass (ljx_force)
+  ljx::Step<T> p = make_step<T>(e, a, l, 1.0);
+  set_pack_rules(p, e->c, m);
+  p.partials = e->partial(kDensityPart);
+  if (m.density == ljx::kDensityHalf) {
+    // Half lists scatter into neighbor rows, ghosts included: start from zero.
+    const long long rows = std::min<long long>(p.nall, e->c.max_atoms);
+    check(cudaMemsetAsync(e->rho, 0, rows * sizeof(T), s), "cudaMemsetAsync(rho)");
+  }
+  launch_density<T>(e, s, p, m.density);
+  e->last_duplicate = m.duplicate ? 2 : 1;
+  return LJX_OK;
+}
+
+template <typename T>
+ljx_status embed_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a)
+{
+  if (e->c.potential != LJX_POTENTIAL_EAM) return LJX_OK;
+  ljx::Step<T> p = make_step<T>(e, a, nullptr, 1.0);
+  p.partials = e->partial(kEmbedPart);
+  if (p.nlocal <= 0) return LJX_OK;
+  const int per = blocks_per_sm(ljx::k_embed<T>);
+  const int need = (p.nlocal + ljx::kBlock - 1) / ljx::kBlock;
+  const int grid = std::max(1, std::min(need, std::min(e->max_grid, e->sm_count * per)));
+  ljx::k_embed<T><<<grid, ljx::kBlock, 0, s>>>(p);
+  check_launch("k_embed");
+  e->launches++;
+  e->step_blocks[kEmbedPart] = grid;
+  return LJX_OK;
+}
+
+template <typename T>
+ljx_status force_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
+                      int newton_pair, double scale)
+{
+  const Modes m = decide_modes(e->c, newton_pair);
+  ljx::Step<T> p = make_step<T>(e, a, l, scale);
+  set_pack_rules(p, e->c, m);
+  e->last_scale = scale;
+  if (e->c.potential == LJX_POTENTIAL_LJ) {
+    p.partials = e->partial(kLjPart);
+    launch_lj<T>(e, s, p, m.lj);
+    e->last_duplicate = m.duplicate ? 2 : 1;
+    return LJX_OK;
+  }
+  p.partials = e->partial(kForcePart);
+  launch_force<T>(e, s, p, m.force);
+  return LJX_OK;
+}
+
+template <typename T>
+ljx_status pack_atoms_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a)
+{
+  ljx::Step<T> p = make_step<T>(e, a, nullptr, 1.0);
+  const int span = std::min(p.nall, e->c.max_atoms);
+  if (span <= 0) return LJX_OK;
+  ljx::k_pack_atoms<T><<<flat_grid(span), ljx::kBlock, 0, s>>>(p, span);
+  check_launch("k_pack_atoms");
+  e->launches++;
+  return LJX_OK;
+}
+
+template <typename S>
+void launch_flat_rows(const char *what, long long items, cudaStream_t s, void (*kernel)(S *, int, const int *, int, int),
+                      S *rows, int width, const int *owner, int first, int n)
+{
+  if (items <= 0) return;
+  kernel<<<flat_grid(items), ljx::kBlock, 0, s>>>(rows, width, owner, first, n);
+  check_launch(what);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *ljx_version(void) { return LJX_VERSION; }
+
+ljx_status ljx_bundle_load(const char *path, ljx_bundle **out)
+{
+  if (path == nullptr || out == nullptr) return LJX_ERR_INVALID;
+  try {
+    auto *b = new ljx_bundle{ljx::load_bundle(path)};
+    *out = b;
+    return LJX_OK;
+  } catch (const std::exception &err) {
+    g_bundle_error = err.what();
+    *out = nullptr;
+    return LJX_ERR_BUNDLE;
+  }
+}
+
+ljx_status ljx_bundle_load_string(const char *json, size_t length, ljx_bundle **out)
+{
+  if (json == nullptr || out == nullptr) return LJX_ERR_INVALID;
+  try {
+    auto *b = new ljx_bundle{ljx::parse_bundle(std::string(json, length))};
+    *out = b;
+    return LJX_OK;
+  } catch (const std::exception &err) {
+    g_bundle_error = err.what();
+    *out = nullptr;
+    return LJX_ERR_BUNDLE;
+  }
+}
+
+const char *ljx_bundle_error(void) { return g_bundle_error.c_str(); }
+
+ljx_status ljx_bundle_contract(const ljx_bundle *bundle, ljx_contract *out)
+{
+  if (bundle == nullptr || out == nullptr) return LJX_ERR_INVALID;
+  *out = bundle->b.contract;
+  return LJX_OK;
+}
+
+ljx_status ljx_bundle_eam_tables(const ljx_bundle *bundle, int *n_elements, int *nrho, int *nr,
+                                 double *drho, double *dr, double *cutoff, double *embedding,
+                                 double *density, double *pair)
+{
+  if (bundle == nullptr) return LJX_ERR_INVALID;
+  const ljx::EamTables &t = bundle->b.eam;
+  if (bundle->b.contract.potential != LJX_POTENTIAL_EAM) return LJX_ERR_INVALID;
+  if (n_elements) *n_elements = t.n_elements;
+  if (nrho) *nrho = t.nrho;
+  if (nr) *nr = t.nr;
+  if (drho) *drho = t.drho;
+  if (dr) *dr = t.dr;
+  if (cutoff) *cutoff = t.cutoff;
+  if (embedding) std::memcpy(embedding, t.embedding.data(), t.embedding.size() * sizeof(double));
+  if (density) std::memcpy(density, t.density.data(), t.density.size() * sizeof(double));
+  if (pair) std::memcpy(pair, t.pair.data(), t.pair.size() * sizeof(double));
+  return LJX_OK;
+}
+
+void ljx_bundle_free(ljx_bundle *bundle) { delete bundle; }
+
+ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **out)
+{
+  if (bundle == nullptr || out == nullptr) return LJX_ERR_INVALID;
+  *out = nullptr;
+  std::unique_ptr<ljx_engine> e(new ljx_engine());
+  e->bundle = bundle->b;
+  e->c = bundle->b.contract;
+  e->device = device;
+  const ljx_contract &c = e->c;
+  if (c.potential == LJX_POTENTIAL_NONE) {
+    g_bundle_error =
+        "LAMMPS-JAX bundle carries no potential block; the ljx engine runs eam/alloy, eam and "
+        "lj/cut bundles written with their potential parameters";
+    return LJX_ERR_UNSUPPORTED;
+  }
+  if (c.n_hops != 1) {
+    g_bundle_error = "ljx runs single-hop (n_hops = 1) bundles; EAM and LJ need one cutoff";
+    return LJX_ERR_UNSUPPORTED;
+  }
+  try {
+    DeviceGuard guard(device);
+    check(cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, device),
+          "cudaDeviceGetAttribute");
+    e->f64 = c.precision == LJX_FLOAT64;
+    const size_t real = e->f64 ? sizeof(double) : sizeof(float);
+    const long long max_atoms = c.max_atoms;
+    const bool matrix = c.input_layout == LJX_LAYOUT_NEIGHBOR_MATRIX;
+    e->rows_cap = c.max_owned > 0 ? c.max_owned : c.max_atoms;
+    e->row_cap = matrix ? c.max_neighbors
+                        : static_cast<int>(std::max<long long>(1, c.max_edges / e->rows_cap));
+    e->max_grid = e->sm_count * 8;
+    e->xd4 = static_cast<double4 *>(device_alloc(max_atoms * sizeof(double4), "cudaMalloc(xd4)"));
+    check(cudaMemset(e->xd4, 0, max_atoms * sizeof(double4)), "cudaMemset(xd4)");
+    if (!e->f64) {
+      e->pos4 = device_alloc(max_atoms * sizeof(float4), "cudaMalloc(pos4)");
+      check(cudaMemset(e->pos4, 0, max_atoms * sizeof(float4)), "cudaMemset(pos4)");
+    }
+    e->rho = device_alloc(max_atoms * real, "cudaMalloc(rho)");
+    e->fp = device_alloc(max_atoms * real, "cudaMalloc(fp)");
+    check(cudaMemset(e->rho, 0, max_atoms * real), "cudaMemset(rho)");
+    check(cudaMemset(e->fp, 0, max_atoms * real), "cudaMemset(fp)");
+    e->cedges = static_cast<int *>(device_alloc(
+        static_cast<size_t>(e->rows_cap) * e->row_cap * sizeof(int), "cudaMalloc(compacted rows)"));
+    e->ccount = static_cast<int *>(device_alloc(e->rows_cap * sizeof(int), "cudaMalloc(counts)"));
+    check(cudaMemset(e->ccount, 0, e->rows_cap * sizeof(int)), "cudaMemset(counts)");
+    e->offsets = static_cast<long long *>(
+        device_alloc((static_cast<size_t>(e->rows_cap) + 1) * sizeof(long long), "cudaMalloc(offsets)"));
+    check(cudaMemset(e->offsets, 0, (static_cast<size_t>(e->rows_cap) + 1) * sizeof(long long)),
+          "cudaMemset(offsets)");
+    e->count_prev = static_cast<long long *>(device_alloc(sizeof(long long), "cudaMalloc(count)"));
+    check(cudaMemset(e->count_prev, 0, sizeof(long long)), "cudaMemset(count)");
+    if (!matrix) {
+      // Padding contract of the sparse edge ABI (cpp/pair_jax_kokkos.cpp:379-383).
+      const size_t me = static_cast<size_t>(c.max_edges);
+      e->senders = static_cast<int *>(device_alloc(me * sizeof(int), "cudaMalloc(senders)"));
+      e->receivers = static_cast<int *>(device_alloc(me * sizeof(int), "cudaMalloc(receivers)"));
+      e->edge_mask = static_cast<uint8_t *>(device_alloc(me, "cudaMalloc(edge_mask)"));
+      std::vector<int> pad(std::min<size_t>(me, 1 << 20), c.max_atoms);
+      for (size_t off = 0; off < me; off += pad.size()) {
+        const size_t n = std::min(pad.size(), me - off);
+        check(cudaMemcpy(e->senders + off, pad.data(), n * sizeof(int), cudaMemcpyHostToDevice),
+              "cudaMemcpy(senders)");
+        check(cudaMemcpy(e->receivers + off, pad.data(), n * sizeof(int), cudaMemcpyHostToDevice),
+              "cudaMemcpy(receivers)");
+      }
+      check(cudaMemset(e->edge_mask, 0, me), "cudaMemset(edge_mask)");
+    }
+    e->partials = static_cast<double *>(device_alloc(
+        4ULL * e->max_grid * ljx::kPartialWidth * sizeof(double), "cudaMalloc(partials)"));
+    check(cudaMemset(e->partials, 0, 4ULL * e->max_grid * ljx::kPartialWidth * sizeof(double)),
+          "cudaMemset(partials)");
+    e->result = static_cast<double *>(device_alloc(16 * sizeof(double), "cudaMalloc(result)"));
+    check(cudaMallocHost(reinterpret_cast<void **>(&e->host_result), 16 * sizeof(double)),
+          "cudaMallocHost(result)");
+    if (c.potential == LJX_POTENTIAL_EAM) {
+      const ljx::EamTables &t = e->bundle.eam;
+      if (e->f64) {
+        e->embedding = upload_table<double>(t.embedding);
+        e->density = upload_table<double>(t.density);
+        e->pair = upload_table<double>(t.pair);
+      } else {
+        e->embedding = upload_table<float>(t.embedding);
+        e->density = upload_table<float>(t.density);
+        e->pair = upload_table<float>(t.pair);
+      }
+    }
+    check(cudaDeviceSynchronize(), "cudaDeviceSynchronize(create)");
+  } catch (const std::exception &err) {
+    g_bundle_error = err.what();
+    return LJX_ERR_CUDA;
+  }
+  *out = e.release();
+  return LJX_OK;
+}
+
+void ljx_engine_destroy(ljx_engine *engine) { delete engine; }
+
+const char *ljx_engine_error(const ljx_engine *engine)
+{
+  return engine ? engine->error.c_str() : "null engine";
+}
+
+ljx_status ljx_engine_plan(ljx_engine *e, int newton_pair, ljx_plan *plan)
+{
+  if (e == nullptr || plan == nullptr) return LJX_ERR_INVALID;
+  // init_style newton checks, cpp/pair_jax_kokkos.cpp:668-673.
+  if (e->c.newton == LJX_NEWTON_ON && !newton_pair)
+    return fail(e, LJX_ERR_INVALID,
+                "LAMMPS-JAX bundle was exported for newton pair on; this run uses newton off");
+  if (e->c.newton == LJX_NEWTON_OFF && newton_pair)
+    return fail(e, LJX_ERR_INVALID,
+                "LAMMPS-JAX bundle was exported for newton pair off; this run uses newton on");
+  const Modes m = decide_modes(e->c, newton_pair);
+  plan->half_list = m.half_list;
+  plan->reverse_density = m.reverse_density;
+  plan->forward_fp = m.forward_fp;
+  plan->reverse_force = m.reverse_force;
+  plan->comm_width = 1;
+  plan->comm_elem_bytes = e->f64 ? 8 : 4;
+  return LJX_OK;
+}
+
+ljx_status ljx_pack_atoms(ljx_engine *e, void *stream, const ljx_atoms *atoms)
+{
+  return guarded(e, [&]() -> ljx_status {
+    if (atoms == nullptr || (atoms->nlocal + atoms->nghost > 0 && (!atoms->x || !atoms->type)))
+      return fail(e, LJX_ERR_INVALID, "atom arrays are incomplete");
+    const ljx_status cap = check_capacity(e, atoms);
+    if (cap != LJX_OK) return cap;
+    for (int &b : e->step_blocks) b = 0;
+    e->last_nlocal = atoms->nlocal;
+    e->last_nall = atoms->nlocal + atoms->nghost;
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? pack_atoms_impl<double>(e, s, atoms) : pack_atoms_impl<float>(e, s, atoms);
+  });
+}
+
+ljx_status ljx_pack_edges(ljx_engine *e, void *stream, const ljx_atoms *atoms,
+                          const ljx_list *list, int newton_pair)
+{
+  return guarded(e, [&]() -> ljx_status {
+    if (e->c.input_layout != LJX_LAYOUT_SPARSE_EDGE)
+      return fail(e, LJX_ERR_INVALID, "neighbor-matrix bundles have no sparse edge arrays");
+    const ljx_status st = check_list(e, list);
+    if (st != LJX_OK) return st;
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? pack_edges_impl<double>(e, s, atoms, list, newton_pair)
+                  : pack_edges_impl<float>(e, s, atoms, list, newton_pair);
+  });
+}
+
+ljx_status ljx_edges(ljx_engine *e, const int **senders, const int **receivers,
+                     const uint8_t **edge_mask, int *capacity)
+{
+  if (e == nullptr) return LJX_ERR_INVALID;
+  if (e->senders == nullptr) return fail(e, LJX_ERR_INVALID, "no sparse edge arrays");
+  if (senders) *senders = e->senders;
+  if (receivers) *receivers = e->receivers;
+  if (edge_mask) *edge_mask = e->edge_mask;
+  if (capacity) *capacity = e->c.max_edges;
+  return LJX_OK;
+}
+
+ljx_status ljx_density(ljx_engine *e, void *stream, const ljx_atoms *atoms,
+                       const ljx_list *list, int newton_pair)
+{
+  return guarded(e, [&]() -> ljx_status {
+    const ljx_status st = check_list(e, list);
+    if (st != LJX_OK) return st;
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? density_impl<double>(e, s, atoms, list, newton_pair)
+                  : density_impl<float>(e, s, atoms, list, newton_pair);
+  });
+}
+
+ljx_status ljx_embed(ljx_engine *e, void *stream, const ljx_atoms *atoms)
+{
+  return guarded(e, [&]() -> ljx_status {
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? embed_impl<double>(e, s, atoms) : embed_impl<float>(e, s, atoms);
+  });
+}
+
+ljx_status ljx_force(ljx_engine *e, void *stream, const ljx_atoms *atoms, const ljx_list *list,
+                     int newton_pair, double scale)
+{
+  return guarded(e, [&]() -> ljx_status {
+    const ljx_status st = check_list(e, list);
+    if (st != LJX_OK) return st;
+    if (atoms == nullptr || atoms->f == nullptr)
+      return fail(e, LJX_ERR_INVALID, "force array is missing");
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? force_impl<double>(e, s, atoms, list, newton_pair, scale)
+                  : force_impl<float>(e, s, atoms, list, newton_pair, scale);
+  });
+}
+
+ljx_status ljx_read_result(ljx_engine *e, void *stream, ljx_result *out)
+{
+  return guarded(e, [&]() -> ljx_status {
+    auto s = static_cast<cudaStream_t>(stream);
+    ljx::PartialSet set{};
+    for (int k = 0; k < 4; ++k) {
+      set.ptr[k] = e->partial(k);
+      set.blocks[k] = e->step_blocks[k];
+    }
+    ljx::k_finalize<<<1, ljx::kBlock, 0, s>>>(set, e->last_scale, e->result);
+    check_launch("k_finalize");
+    e->launches++;
+    check(cudaMemcpyAsync(e->host_result, e->result, 9 * sizeof(double), cudaMemcpyDeviceToHost, s),
+          "cudaMemcpyAsync(result)");
+    check(cudaStreamSynchronize(s), "cudaStreamSynchronize(result)");
+    const double *r = e->host_result;
+    ljx_result res{};
+    res.energy = r[0];
+    for (int k = 0; k < 6; ++k) res.virial[k] = r[1 + k];
+    res.edge_count = static_cast<long long>(r[7]) * e->last_duplicate;
+    res.widest_row = static_cast<int>(r[8]);
+    if (e->c.input_layout == LJX_LAYOUT_NEIGHBOR_MATRIX)
+      res.overflow = res.widest_row > e->c.max_neighbors;
+    else
+      res.overflow = res.edge_count > e->c.max_edges;
+    if (out) *out = res;
+    for (int &b : e->step_blocks) b = 0;
+    return LJX_OK;
+  });
+}
+
+ljx_status ljx_feature_rows(ljx_engine *e, int which, void **rows, int *width, int *elem_bytes)
+{
+  if (e == nullptr || rows == nullptr) return LJX_ERR_INVALID;
+  if (which != 0 && which != 1) return fail(e, LJX_ERR_INVALID, "feature must be 0 (rho) or 1 (F')");
+  *rows = which == 0 ? e->rho : e->fp;
+  if (width) *width = 1;
+  if (elem_bytes) *elem_bytes = e->f64 ? 8 : 4;
+  return LJX_OK;
+}
+
+long long ljx_engine_launches(const ljx_engine *e) { return e ? e->launches : 0; }
+
+// ---- comm rows ----
+
+static ljx_status comm_status(cudaError_t err)
+{
+  return err == cudaSuccess ? LJX_OK : LJX_ERR_CUDA;
+}
+
+ljx_status ljx_comm_pack_forward(void *stream, const void *rows, int words, const int *sendlist,
+                                 int n, double *buf, int slots)
+{
+  if (n <= 0) return LJX_OK;
+  if (!rows || !sendlist || !buf || words <= 0 || slots * 2 < words) return LJX_ERR_INVALID;
+  ljx::k_pack_words_by_list<<<flat_grid(static_cast<long long>(n) * words), ljx::kBlock, 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint32_t *>(rows), words, sendlist, n, buf, slots);
+  return comm_status(cudaGetLastError());
+}
+
+ljx_status ljx_comm_unpack_forward(void *stream, void *rows, int words, int first, int n,
+                                   const double *buf, int slots)
+{
+  if (n <= 0) return LJX_OK;
+  if (!rows || !buf || words <= 0 || slots * 2 < words) return LJX_ERR_INVALID;
+  ljx::k_unpack_words_at<<<flat_grid(static_cast<long long>(n) * words), ljx::kBlock, 0,
+                           static_cast<cudaStream_t>(stream)>>>(static_cast<uint32_t *>(rows),
+                                                                words, first, n, buf, slots);
+  return comm_status(cudaGetLastError());
+}
+
+ljx_status ljx_comm_pack_reverse(void *stream, const void *rows, int words, int first, int n,
+                                 double *buf, int slots)
+{
+  if (n <= 0) return LJX_OK;
+  if (!rows || !buf || words <= 0 || slots * 2 < words) return LJX_ERR_INVALID;
+  ljx::k_pack_words_at<<<flat_grid(static_cast<long long>(n) * words), ljx::kBlock, 0,
+                         static_cast<cudaStream_t>(stream)>>>(static_cast<const uint32_t *>(rows),
+                                                              words, first, n, buf, slots);
+  return comm_status(cudaGetLastError());
+}
+
+ljx_status ljx_comm_unpack_reverse(void *stream, void *rows, int width, int elem_bytes,
+                                   const int *sendlist, int n, const double *buf, int slots)
+{
+  if (n <= 0) return LJX_OK;
+  if (!rows || !sendlist || !buf || width <= 0) return LJX_ERR_INVALID;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int grid = flat_grid(static_cast<long long>(n) * width);
+  if (elem_bytes == 8)
+    ljx::k_add_rows_by_list<double><<<grid, ljx::kBlock, 0, s>>>(static_cast<double *>(rows),
+                                                                 width, sendlist, n, buf, slots);
+  else if (elem_bytes == 4)
+    ljx::k_add_rows_by_list<float><<<grid, ljx::kBlock, 0, s>>>(static_cast<float *>(rows), width,
+                                                                sendlist, n, buf, slots);
+  else
+    return LJX_ERR_INVALID;
+  return comm_status(cudaGetLastError());
+}
+
+ljx_status ljx_comm_zero_rows(void *stream, void *rows, int width, int elem_bytes, int first,
+                              int n)
+{
+  if (n <= 0) return LJX_OK;
+  if (!rows || width <= 0) return LJX_ERR_INVALID;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int grid = flat_grid(static_cast<long long>(n) * width);
+  if (elem_bytes == 8)
+    ljx::k_zero_rows<double><<<grid, ljx::kBlock, 0, s>>>(static_cast<double *>(rows), width, first, n);
+  else if (elem_bytes == 4)
+    ljx::k_zero_rows<float><<<grid, ljx::kBlock, 0, s>>>(static_cast<float *>(rows), width, first, n);
+  else
+    return LJX_ERR_INVALID;
+  return comm_status(cudaGetLastError());
+}
+
+ljx_status ljx_halo_forward_self(void *stream, void *rows, int width, int elem_bytes,
+                                 const int *owner, int first, int n)
+{
+  if (n <= 0) return LJX_OK;
+  if (!rows || !owner || width <= 0) return LJX_ERR_INVALID;
+  auto s = static_cast<cudaStream_t>(stream);
+  const long long items = static_cast<long long>(n) * width;
+  try {
+    if (elem_bytes == 8)
+      launch_flat_rows<double>("k_forward_self", items, s, ljx::k_forward_self<double>,
+                               static_cast<double *>(rows), width, owner, first, n);
+    else if (elem_bytes == 4)
+      launch_flat_rows<float>("k_forward_self", items, s, ljx::k_forward_self<float>,
+                              static_cast<float *>(rows), width, owner, first, n);
+    else
+      return LJX_ERR_INVALID;
+  } catch (const std::exception &) {
+    return LJX_ERR_CUDA;
+  }
+  return LJX_OK;
+}
+
+ljx_status ljx_halo_reverse_self(void *stream, void *rows, int width, int elem_bytes,
+                                 const int *owner, int first, int n)
+{
+  if (n <= 0) return LJX_OK;
+  if (!rows || !owner || width <= 0) return LJX_ERR_INVALID;
+  auto s = static_cast<cudaStream_t>(stream);
+  const long long items = static_cast<long long>(n) * width;
+  try {
+    if (elem_bytes == 8)
+      launch_flat_rows<double>("k_reverse_self", items, s, ljx::k_reverse_self<double>,
+                               static_cast<double *>(rows), width, owner, first, n);
+    else if (elem_bytes == 4)
+      launch_flat_rows<float>("k_reverse_self", items, s, ljx::k_reverse_self<float>,
+                              static_cast<float *>(rows), width, owner, first, n);
+    else
+      return LJX_ERR_INVALID;
+  } catch (const std::exception &) {
+    return LJX_ERR_CUDA;
+  }
+  return LJX_OK;
+}
+
+}  // extern "C"

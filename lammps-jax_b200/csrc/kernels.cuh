@@ -1,0 +1,730 @@
+// Device kernels of the ljx engine (sm_100a). One warp owns one LAMMPS list row at a time
+// ("warp per row"): lanes take consecutive slots, a ballot compacts the kept pairs, per-row sums
+// finish with warp shuffles, and only scatters to a neighbor's row (half lists, newton-on ghost
+// rows) use atomics. Grids are persistent: a multiple of the SM count, warps stride over rows.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ljx {
+
+constexpr int kWarp = 32;
+constexpr int kBlock = 256;
+constexpr int kWarpsPerBlock = kBlock / kWarp;
+constexpr unsigned kFull = 0xffffffffu;
+// LAMMPS keeps special-bond flags in the top bits of neighbor indices.
+constexpr int kNeighMask = 0x1FFFFFFF;
+// One block's partial sums: [0] energy, [1..6] virial, [7] kept pairs, [8] widest row (max).
+constexpr int kPartialWidth = 10;
+
+enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2 };
+// Force distribution modes.
+//  kRowsFull : full list, newton off; row i takes the whole pair force, no scatter.
+//  kGhost    : full list, newton on, plain bundle; each edge carries F'(rho_i) rho_j' + phi'/2
+//              to both endpoints (the autodiff of the plain energy program).
+//  kHalf     : half list, newton on; whole pair force, sender +, receiver -.
+enum ForceMode { kRowsFull = 0, kGhost = 1, kHalf = 2 };
+enum LjMode { kLjEdgeFull = 0, kLjEdgeHalf = 1, kLjAtomFull = 2, kLjAtomHalfPairSum = 3 };
+
+template <typename T> struct Vec4;
+template <> struct Vec4<float> { using type = float4; };
+template <> struct Vec4<double> { using type = double4; };
+
+__device__ __forceinline__ double4 load4(const double4 *p)
+{
+  const double2 a = __ldg(reinterpret_cast<const double2 *>(p));
+  const double2 b = __ldg(reinterpret_cast<const double2 *>(p) + 1);
+  return make_double4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float4 load4(const float4 *p) { return __ldg(p); }
+
+template <typename T>
+struct Step {
+  // LAMMPS arrays.
+  const double *x;
+  const int *type;
+  double *f;
+  int nlocal;
+  int nghost;
+  int nall;
+  // LAMMPS list.
+  const int *ilist;
+  const int *numneigh;
+  const int *neighbors;
+  long long atom_stride;
+  long long slot_stride;
+  int inum;
+  int maxneighs;
+  // Engine buffers.
+  double4 *xd4;                       // x, y, z, species (double), rows < max_atoms
+  typename Vec4<T>::type *pos4;       // contract-precision copy (float runs only)
+  T *rho;
+  T *fp;
+  int *cedges;                        // compacted rows: row * row_cap + slot
+  int *ccount;                        // kept pairs per row (may exceed row_cap: spilled row)
+  int row_cap;
+  // Tables: [n_el][n][4] at contract precision.
+  const typename Vec4<T>::type *embedding;
+  const typename Vec4<T>::type *density;
+  const typename Vec4<T>::type *pair;
+  int nrho;
+  int nr;
+  T drho;
+  T inv_dr;
+  // Cutoffs: the pack filter is the reference's double test (r^2 <= rc^2 from LAMMPS x); the
+  // model keeps r^2 < rc^2 at contract precision.
+  double pack_cutsq;
+  T model_cutsq;
+  int max_atoms;
+  int half_rule;                      // drop j < i (half-edge bundle on a full list)
+  int unique_rule;                    // keep a ghost j only if it sorts after i in (z, y, x)
+  double scale;
+  // LJ.
+  T lj_four_eps;
+  T lj_sigma_sq;
+  T lj_energy_scale;
+  // Per-block partial sums.
+  double *partials;
+};
+
+__device__ __forceinline__ double warp_sum(double v)
+{
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Reduce the thread's {energy, virial[6], kept} sums and widest row over the block and store
+// one partial row (every slot written, so the finalize step can sum all kernels uniformly).
+__device__ __forceinline__ void store_partials(double (&v)[8], int widest, double *partials)
+{
+  __shared__ double sm[kWarpsPerBlock][9];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = warp_sum(v[k]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) widest = max(widest, __shfl_xor_sync(kFull, widest, o));
+  if (lane == 0) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sm[warp][k] = v[k];
+    sm[warp][8] = static_cast<double>(widest);
+  }
+  __syncthreads();
+  if (threadIdx.x < kPartialWidth) {
+    const int k = threadIdx.x;
+    double s = 0.0;
+    if (k < 8) {
+      for (int w = 0; w < kWarpsPerBlock; ++w) s += sm[w][k];
+    } else if (k == 8) {
+      for (int w = 0; w < kWarpsPerBlock; ++w) s = fmax(s, sm[w][8]);
+    }
+    partials[static_cast<long long>(blockIdx.x) * kPartialWidth + k] = s;
+  }
+}
+
+// Value and slope of one spline table at x (python/lammps_jax/eam.py:138-164 without
+// extrapolation): node = clip(floor(x/delta), 0, n-2), t = min(x/delta - node, 1).
+template <typename T>
+__device__ __forceinline__ void spline_vs(const typename Vec4<T>::type *tab, int n, T x,
+                                          T inv_delta, T &v, T &s)
+{
+  const T idx = x * inv_delta;
+  T fl = floor(idx);
+  fl = fmin(fmax(fl, T(0)), T(n - 2));
+  const T t = fmin(idx - fl, T(1));
+  const auto c = load4(tab + static_cast<int>(fl));
+  v = c.x + t * (c.y + t * (c.z + t * c.w));
+  s = (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * inv_delta;
+}
+
+template <typename T>
+__device__ __forceinline__ T spline_v(const typename Vec4<T>::type *tab, int n, T x, T inv_delta)
+{
+  const T idx = x * inv_delta;
+  T fl = floor(idx);
+  fl = fmin(fmax(fl, T(0)), T(n - 2));
+  const T t = fmin(idx - fl, T(1));
+  const auto c = load4(tab + static_cast<int>(fl));
+  return c.x + t * (c.y + t * (c.z + t * c.w));
+}
+
+template <typename T>
+__device__ __forceinline__ T spline_s(const typename Vec4<T>::type *tab, int n, T x, T inv_delta)
+{
+  const T idx = x * inv_delta;
+  T fl = floor(idx);
+  fl = fmin(fmax(fl, T(0)), T(n - 2));
+  const T t = fmin(idx - fl, T(1));
+  const auto c = load4(tab + static_cast<int>(fl));
+  return (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * inv_delta;
+}
+
+__device__ __forceinline__ int pair_row(int a, int b)
+{
+  const int hi = a > b ? a : b, lo = a > b ? b : a;
+  return hi * (hi + 1) / 2 + lo;
+}
+
+// The reference's distance filter and pairing rules for list slot (i -> j),
+// cpp/pair_jax_kokkos.cpp:84-101. r^2 is formed without fused multiply-adds so it is the same
+// double the reference computes.
+template <typename T>
+__device__ __forceinline__ bool pack_keep(const Step<T> &p, int i, const double4 &xi, int j,
+                                          const double4 &xj)
+{
+  const double dx = __dsub_rn(xi.x, xj.x);
+  const double dy = __dsub_rn(xi.y, xj.y);
+  const double dz = __dsub_rn(xi.z, xj.z);
+  const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
+  if (r2 > p.pack_cutsq) return false;
+  if (p.half_rule && j < i) return false;
+  if (p.unique_rule && j >= p.nlocal) {
+    if (xj.z < xi.z) return false;
+    if (xj.z == xi.z) {
+      if (xj.y < xi.y) return false;
+      if (xj.y == xi.y && xj.x < xi.x) return false;
+    }
+  }
+  return true;
+}
+
+// a1: LAMMPS x/type -> xd4 (and the float copy): cpp/pair_jax_kokkos.cpp:35-52.
+template <typename T>
+__global__ void __launch_bounds__(kBlock) k_pack_atoms(const Step<T> p, int span)
+{
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < span; i += gridDim.x * blockDim.x) {
+    const double x0 = p.x[3 * i], x1 = p.x[3 * i + 1], x2 = p.x[3 * i + 2];
+    const int s = p.type[i] - 1;
+    p.xd4[i] = make_double4(x0, x1, x2, static_cast<double>(s));
+    if (p.pos4 != nullptr) {
+      reinterpret_cast<float4 *>(p.pos4)[i] =
+          make_float4(static_cast<float>(x0), static_cast<float>(x1), static_cast<float>(x2),
+                      static_cast<float>(s));
+    }
+  }
+}
+
+// a2 + a6: filter and compact each list row, accumulating the EAM density.
+// partials[block] = {kept pairs, widest row, ...}.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
+{
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  double kept_sum = 0.0;
+  int widest = 0;
+  for (int row = blockIdx.x * kWarpsPerBlock + warp; row < p.inum;
+       row += gridDim.x * kWarpsPerBlock) {
+    const int i = p.ilist[row];
+    if (i >= p.max_atoms) {
+      if (lane == 0) p.ccount[row] = 0;
+      continue;
+    }
+    const int listed = p.numneigh[i];
+    widest = max(widest, listed);
+    const int n = min(listed, p.maxneighs);
+    const double4 xi = load4(p.xd4 + i);
+    const int si = static_cast<int>(xi.w);
+    int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
+    const long long rowbase = static_cast<long long>(i) * p.atom_stride;
+    T rho = T(0);
+    int kept = 0;
+    for (int base = 0; base < n; base += kWarp) {
+      const int jj = base + lane;
+      int j = 0;
+      bool keep = false;
+      double4 xj = make_double4(0, 0, 0, 0);
+      if (jj < n) {
+        j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
+        if (j < p.max_atoms) {
+          xj = load4(p.xd4 + j);
+          keep = pack_keep(p, i, xi, j, xj);
+        }
+      }
+      const unsigned m = __ballot_sync(kFull, keep);
+      if (keep) {
+        const int slot = kept + __popc(m & below);
+        if (slot < p.row_cap) crow[slot] = j;
+        if (MODE != kCompactOnly) {
+          const T dx = T(xj.x) - T(xi.x), dy = T(xj.y) - T(xi.y), dz = T(xj.z) - T(xi.z);
+          const T r2 = dx * dx + dy * dy + dz * dz;
+          if (r2 < p.model_cutsq) {
+            const T r = sqrt(r2);
+            const int sj = static_cast<int>(xj.w);
+            rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+            if (MODE == kDensityHalf)
+              atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+          }
+        }
+      }
+      kept += __popc(m);
+    }
+    if (MODE != kCompactOnly) {
+      rho = warp_sum(rho);
+      if (lane == 0) {
+        if (MODE == kDensityHalf)
+          atomicAdd(p.rho + i, rho);
+        else
+          p.rho[i] = rho;
+      }
+    }
+    if (lane == 0) p.ccount[row] = kept;
+    kept_sum += kept;
+  }
+  // kept_sum is carried by lane 0 of each warp (the other lanes hold copies): count it once.
+  double acc[8] = {0, 0, 0, 0, 0, 0, 0, lane == 0 ? kept_sum : 0.0};
+  store_partials(acc, widest, p.partials);
+}
+
+// a8: F(rho) and F'(rho) of owned rows with linear continuation past rhomax
+// (python/lammps_jax/eam.py:138-164 with extrapolate, :319-321, :383-384).
+template <typename T>
+__global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
+{
+  double e = 0.0;
+  const T inv_drho = T(1) / p.drho;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.nlocal;
+       i += gridDim.x * blockDim.x) {
+    const int s = p.type[i] - 1;
+    const T rho = p.rho[i];
+    const T idx = rho / p.drho;
+    T fl = floor(idx);
+    fl = fmin(fmax(fl, T(0)), T(p.nrho - 2));
+    const T t_raw = idx - fl;
+    const T t = fmin(t_raw, T(1));
+    const auto c = load4(p.embedding + s * p.nrho + static_cast<int>(fl));
+    const T end = c.y + T(2) * c.z + T(3) * c.w;
+    T v = c.x + t * (c.y + t * (c.z + t * c.w));
+    v = v + (t_raw - t) * end;
+    T sl = c.y + t * (T(2) * c.z + t * (T(3) * c.w));
+    if (t_raw > t) sl = end;
+    p.fp[i] = sl * inv_drho;
+    e += static_cast<double>(v);
+  }
+  double acc[8] = {e, 0, 0, 0, 0, 0, 0, 0};
+  store_partials(acc, 0, p.partials);
+}
+
+// One EAM edge (i -> j) of the force pass; python/lammps_jax/eam.py:383-398 for the pair force
+// and :300-309 for the pair energy. Accumulates the row's force and the thread's energy/virial.
+template <typename T, int MODE>
+__device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T>::type &pi,
+                                         int si, T fpi, int j, T &fx, T &fy, T &fz, double &e,
+                                         double (&v)[6])
+{
+  typename Vec4<T>::type pj;
+  if constexpr (sizeof(T) == 8) {
+    pj = load4(p.xd4 + j);
+  } else {
+    pj = load4(p.pos4 + j);
+  }
+  const T dx = pj.x - pi.x, dy = pj.y - pi.y, dz = pj.z - pi.z;
+  const T r2 = dx * dx + dy * dy + dz * dz;
+  if (!(r2 < p.model_cutsq)) return;
+  const T r = sqrt(r2);
+  const T rinv = T(1) / r;
+  const int sj = static_cast<int>(pj.w);
+  const T rhojp = spline_s<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+  T z2, z2p;
+  spline_vs<T>(p.pair + pair_row(si, sj) * p.nr, p.nr, r, p.inv_dr, z2, z2p);
+  const T phi = z2 * rinv;
+  const T phip = (z2p - phi) * rinv;
+  T psip;
+  if (MODE == kGhost) {
+    psip = fpi * rhojp + T(0.5) * phip;
+  } else {
+    const T rhoip = (si == sj) ? rhojp : spline_s<T>(p.density + si * p.nr, p.nr, r, p.inv_dr);
+    psip = fpi * rhojp + __ldg(p.fp + j) * rhoip + phip;
+  }
+  const T sc = psip * rinv;
+  const T ex = sc * dx, ey = sc * dy, ez = sc * dz;
+  fx += ex;
+  fy += ey;
+  fz += ez;
+  e += static_cast<double>(MODE == kHalf ? phi : T(0.5) * phi);
+  const double w = MODE == kRowsFull ? 0.5 : 1.0;
+  v[0] -= w * static_cast<double>(dx * ex);
+  v[1] -= w * static_cast<double>(dy * ey);
+  v[2] -= w * static_cast<double>(dz * ez);
+  v[3] -= w * static_cast<double>(dx * ey);
+  v[4] -= w * static_cast<double>(dx * ez);
+  v[5] -= w * static_cast<double>(dy * ez);
+  if (MODE != kRowsFull) {
+    atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
+    atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
+    atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
+  }
+}
+
+// a9..a13: fused force + pair energy + virial over the compacted rows. Spilled rows (more kept
+// pairs than row_cap) re-walk the LAMMPS list with the same filter.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
+{
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double e = 0.0;
+  double v[6] = {0, 0, 0, 0, 0, 0};
+  for (int row = blockIdx.x * kWarpsPerBlock + warp; row < p.inum;
+       row += gridDim.x * kWarpsPerBlock) {
+    const int i = p.ilist[row];
+    if (i >= p.max_atoms) continue;
+    const int n = p.ccount[row];
+    typename Vec4<T>::type pi;
+    if constexpr (sizeof(T) == 8) {
+      pi = load4(p.xd4 + i);
+    } else {
+      pi = load4(p.pos4 + i);
+    }
+    const int si = static_cast<int>(pi.w);
+    const T fpi = p.fp[i];
+    T fx = T(0), fy = T(0), fz = T(0);
+    if (n <= p.row_cap) {
+      const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
+      for (int k = lane; k < n; k += kWarp) eam_edge<T, MODE>(p, pi, si, fpi, crow[k], fx, fy, fz, e, v);
+    } else {
+      const double4 xi = load4(p.xd4 + i);
+      const int listed = min(p.numneigh[i], p.maxneighs);
+      const long long rowbase = static_cast<long long>(i) * p.atom_stride;
+      for (int jj = lane; jj < listed; jj += kWarp) {
+        const int j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
+        if (j >= p.max_atoms) continue;
+        if (pack_keep(p, i, xi, j, load4(p.xd4 + j)))
+          eam_edge<T, MODE>(p, pi, si, fpi, j, fx, fy, fz, e, v);
+      }
+    }
+    fx = warp_sum(fx);
+    fy = warp_sum(fy);
+    fz = warp_sum(fz);
+    if (lane == 0) {
+      double *fi = p.f + 3 * i;
+      if (MODE == kRowsFull) {
+        fi[0] += p.scale * static_cast<double>(fx);
+        fi[1] += p.scale * static_cast<double>(fy);
+        fi[2] += p.scale * static_cast<double>(fz);
+      } else {
+        atomicAdd(fi + 0, p.scale * static_cast<double>(fx));
+        atomicAdd(fi + 1, p.scale * static_cast<double>(fy));
+        atomicAdd(fi + 2, p.scale * static_cast<double>(fz));
+      }
+    }
+  }
+  double acc[8] = {e, v[0], v[1], v[2], v[3], v[4], v[5], 0.0};
+  store_partials(acc, 0, p.partials);
+}
+
+// LJ 12-6 in one pass over the LAMMPS list: examples/export_model.py:16-74 with the force-add
+// conventions of cpp/pair_jax_kokkos.cpp:176-225.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
+{
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double e = 0.0, kept_sum = 0.0;
+  double v[6] = {0, 0, 0, 0, 0, 0};
+  int widest = 0;
+  const bool scatter = MODE != kLjEdgeFull;
+  // Sender weight (edge-force bundles add dU/drij; atom-force bundles the energy-scaled
+  // gradient, doubled for pair-sum half lists that stand for both directions).
+  const T fw = MODE == kLjAtomFull ? p.lj_energy_scale
+               : MODE == kLjAtomHalfPairSum ? T(2) * p.lj_energy_scale
+                                            : T(1);
+  const T ew = MODE == kLjAtomHalfPairSum ? T(2) * p.lj_energy_scale : p.lj_energy_scale;
+  const double vw = scatter ? 1.0 : 0.5;
+  for (int row = blockIdx.x * kWarpsPerBlock + warp; row < p.inum;
+       row += gridDim.x * kWarpsPerBlock) {
+    const int i = p.ilist[row];
+    if (i >= p.max_atoms) continue;
+    const int listed = p.numneigh[i];
+    widest = max(widest, listed);
+    const int n = min(listed, p.maxneighs);
+    const double4 xi = load4(p.xd4 + i);
+    const long long rowbase = static_cast<long long>(i) * p.atom_stride;
+    T fx = T(0), fy = T(0), fz = T(0);
+    int kept = 0;
+    for (int base = 0; base < n; base += kWarp) {
+      const int jj = base + lane;
+      bool keep = false;
+      int j = 0;
+      double4 xj = make_double4(0, 0, 0, 0);
+      if (jj < n) {
+        j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
+        if (j < p.max_atoms) {
+          xj = load4(p.xd4 + j);
+          keep = pack_keep(p, i, xi, j, xj);
+        }
+      }
+      kept += __popc(__ballot_sync(kFull, keep));
+      if (!keep) continue;
+      const T dx = T(xj.x) - T(xi.x), dy = T(xj.y) - T(xi.y), dz = T(xj.z) - T(xi.z);
+      const T r2 = dx * dx + dy * dy + dz * dz;
+      if (!(r2 > T(1.0e-12) && r2 < p.model_cutsq)) continue;
+      const T inv_r2 = p.lj_sigma_sq / r2;
+      const T inv_r6 = inv_r2 * inv_r2 * inv_r2;
+      const T u = p.lj_four_eps * (inv_r6 * inv_r6 - inv_r6);
+      // dU/drij = 2 rij dU/d(r^2), dU/d(r^2) = -4 eps (6 a^6 - 3 a^3) / r^2, a = sigma^2/r^2.
+      const T g = T(-2) * p.lj_four_eps * (T(6) * inv_r6 * inv_r6 - T(3) * inv_r6) / r2 * fw;
+      const T ex = g * dx, ey = g * dy, ez = g * dz;
+      fx += ex;
+      fy += ey;
+      fz += ez;
+      e += static_cast<double>(ew * u);
+      v[0] -= vw * static_cast<double>(dx * ex);
+      v[1] -= vw * static_cast<double>(dy * ey);
+      v[2] -= vw * static_cast<double>(dz * ez);
+      v[3] -= vw * static_cast<double>(dx * ey);
+      v[4] -= vw * static_cast<double>(dx * ez);
+      v[5] -= vw * static_cast<double>(dy * ez);
+      if (scatter) {
+        atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
+        atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
+        atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
+      }
+    }
+    fx = warp_sum(fx);
+    fy = warp_sum(fy);
+    fz = warp_sum(fz);
+    if (lane == 0) {
+      double *fi = p.f + 3 * i;
+      if (!scatter) {
+        fi[0] += p.scale * static_cast<double>(fx);
+        fi[1] += p.scale * static_cast<double>(fy);
+        fi[2] += p.scale * static_cast<double>(fz);
+      } else {
+        atomicAdd(fi + 0, p.scale * static_cast<double>(fx));
+        atomicAdd(fi + 1, p.scale * static_cast<double>(fy));
+        atomicAdd(fi + 2, p.scale * static_cast<double>(fz));
+      }
+    }
+    kept_sum += kept;
+  }
+  double acc[8] = {e, v[0], v[1], v[2], v[3], v[4], v[5], lane == 0 ? kept_sum : 0.0};
+  store_partials(acc, widest, p.partials);
+}
+
+// Row counts -> exclusive offsets for the reference edge ABI (single block; off the hot path).
+__global__ void k_scan_counts(const int *counts, int n, int per_pair, long long *offsets)
+{
+  __shared__ long long s_part[1024];
+  const int t = threadIdx.x, nt = blockDim.x;
+  const long long chunk = (static_cast<long long>(n) + nt - 1) / nt;
+  const long long lo = chunk * t;
+  const long long hi = lo + chunk < n ? lo + chunk : n;
+  long long sum = 0;
+  for (long long k = lo; k < hi; ++k) sum += static_cast<long long>(counts[k]) * per_pair;
+  s_part[t] = sum;
+  __syncthreads();
+  if (t == 0) {
+    long long run = 0;
+    for (int q = 0; q < nt; ++q) {
+      const long long c = s_part[q];
+      s_part[q] = run;
+      run += c;
+    }
+    offsets[n] = run;
+  }
+  __syncthreads();
+  long long run = s_part[t];
+  for (long long k = lo; k < hi; ++k) {
+    offsets[k] = run;
+    run += static_cast<long long>(counts[k]) * per_pair;
+  }
+}
+
+// Scatter compacted rows into the reference ABI: senders/receivers/edge_mask at the row's
+// offset, duplicated reversed when the bundle asks (cpp/pair_jax_kokkos.cpp:103-116). Rows that
+// spilled past row_cap re-walk the list with the same filter.
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+k_emit_edges(const Step<T> p, const long long *offsets, int duplicate, int max_edges,
+             int *senders, int *receivers, uint8_t *mask)
+{
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  const int per = duplicate ? 2 : 1;
+  for (int row = blockIdx.x * kWarpsPerBlock + warp; row < p.inum;
+       row += gridDim.x * kWarpsPerBlock) {
+    const int i = p.ilist[row];
+    if (i >= p.max_atoms) continue;
+    const int n = p.ccount[row];
+    const long long base_edge = offsets[row];
+    auto put = [&](long long edge, int j) {
+      if (edge + per > max_edges) return;
+      senders[edge] = i;
+      receivers[edge] = j;
+      mask[edge] = 1;
+      if (duplicate) {
+        senders[edge + 1] = j;
+        receivers[edge + 1] = i;
+        mask[edge + 1] = 1;
+      }
+    };
+    if (n <= p.row_cap) {
+      const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
+      for (int k = lane; k < n; k += kWarp) put(base_edge + static_cast<long long>(k) * per, crow[k]);
+    } else {
+      const double4 xi = load4(p.xd4 + i);
+      const int listed = min(p.numneigh[i], p.maxneighs);
+      const long long rowbase = static_cast<long long>(i) * p.atom_stride;
+      int kept = 0;
+      for (int base = 0; base < listed; base += kWarp) {
+        const int jj = base + lane;
+        bool keep = false;
+        int j = 0;
+        if (jj < listed) {
+          j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
+          if (j < p.max_atoms) keep = pack_keep(p, i, xi, j, load4(p.xd4 + j));
+        }
+        const unsigned m = __ballot_sync(kFull, keep);
+        if (keep) put(base_edge + static_cast<long long>(kept + __popc(m & below)) * per, j);
+        kept += __popc(m);
+      }
+    }
+  }
+}
+
+// Padding past the new count up to the previous count (ResetEdgeTailFunctor,
+// cpp/pair_jax_kokkos.cpp:157-173); both counts are read on the device.
+__global__ void k_reset_tail(const long long *count_now, long long *count_prev, int max_atoms,
+                             int max_edges, int *senders, int *receivers, uint8_t *mask)
+{
+  const long long now = *count_now;
+  const long long prev = *count_prev;
+  const long long hi = prev < max_edges ? prev : max_edges;
+  for (long long e = now + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < hi;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    senders[e] = max_atoms;
+    receivers[e] = max_atoms;
+    mask[e] = 0;
+  }
+}
+
+__global__ void k_store_prev(const long long *count_now, long long *count_prev)
+{
+  *count_prev = *count_now;
+}
+
+// Step totals from the per-block partials of the kernels that ran, in a fixed order.
+// result: [0] energy, [1..6] virial (both times `scale`), [7] kept pairs, [8] widest row.
+struct PartialSet {
+  const double *ptr[4];
+  int blocks[4];
+};
+
+__global__ void __launch_bounds__(kBlock) k_finalize(PartialSet set, double scale, double *result)
+{
+  __shared__ double s[9][kBlock];
+  const int t = threadIdx.x;
+  double acc[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  for (int q = 0; q < 4; ++q) {
+    for (int b = t; b < set.blocks[q]; b += blockDim.x) {
+      const double *row = set.ptr[q] + static_cast<long long>(b) * kPartialWidth;
+      for (int k = 0; k < 8; ++k) acc[k] += row[k];
+      acc[8] = fmax(acc[8], row[8]);
+    }
+  }
+  for (int k = 0; k < 9; ++k) s[k][t] = acc[k];
+  __syncthreads();
+  if (t < 9) {
+    double total = 0.0;
+    for (int q = 0; q < static_cast<int>(blockDim.x); ++q)
+      total = (t == 8) ? fmax(total, s[t][q]) : total + s[t][q];
+    result[t] = (t < 7) ? scale * total : total;
+  }
+}
+
+// ---- comm rows (cpp/pair_jax_kokkos.cpp:247-318) ----
+
+__global__ void k_pack_words_by_list(const uint32_t *rows, int words, const int *sendlist, int n,
+                                     double *buf, int slots)
+{
+  const long long total = static_cast<long long>(n) * words;
+  for (long long flat = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; flat < total;
+       flat += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(flat / words), w = static_cast<int>(flat % words);
+    uint32_t *packed = reinterpret_cast<uint32_t *>(buf + static_cast<long long>(i) * slots);
+    packed[w] = rows[static_cast<long long>(sendlist[i]) * words + w];
+    if ((words & 1) && w + 1 == words) packed[words] = 0u;
+  }
+}
+
+__global__ void k_unpack_words_at(uint32_t *rows, int words, int first, int n, const double *buf,
+                                  int slots)
+{
+  const long long total = static_cast<long long>(n) * words;
+  for (long long flat = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; flat < total;
+       flat += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(flat / words), w = static_cast<int>(flat % words);
+    rows[static_cast<long long>(first + i) * words + w] =
+        reinterpret_cast<const uint32_t *>(buf + static_cast<long long>(i) * slots)[w];
+  }
+}
+
+__global__ void k_pack_words_at(const uint32_t *rows, int words, int first, int n, double *buf,
+                                int slots)
+{
+  const long long total = static_cast<long long>(n) * words;
+  for (long long flat = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; flat < total;
+       flat += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(flat / words), w = static_cast<int>(flat % words);
+    uint32_t *packed = reinterpret_cast<uint32_t *>(buf + static_cast<long long>(i) * slots);
+    packed[w] = rows[static_cast<long long>(first + i) * words + w];
+    if ((words & 1) && w + 1 == words) packed[words] = 0u;
+  }
+}
+
+template <typename S>
+__global__ void k_add_rows_by_list(S *rows, int width, const int *sendlist, int n,
+                                   const double *buf, int slots)
+{
+  const long long total = static_cast<long long>(n) * width;
+  for (long long flat = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; flat < total;
+       flat += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(flat / width), w = static_cast<int>(flat % width);
+    // sendlist rows are unique within one swap, so the add needs no atomic.
+    rows[static_cast<long long>(sendlist[i]) * width + w] +=
+        reinterpret_cast<const S *>(buf + static_cast<long long>(i) * slots)[w];
+  }
+}
+
+template <typename S>
+__global__ void k_zero_rows(S *rows, int width, int first, int n)
+{
+  const long long total = static_cast<long long>(n) * width;
+  for (long long flat = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; flat < total;
+       flat += static_cast<long long>(gridDim.x) * blockDim.x)
+    rows[static_cast<long long>(first) * width + flat] = S(0);
+}
+
+template <typename S>
+__global__ void k_forward_self(S *rows, int width, const int *owner, int first, int n)
+{
+  const long long total = static_cast<long long>(n) * width;
+  for (long long flat = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; flat < total;
+       flat += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(flat / width), w = static_cast<int>(flat % width);
+    rows[static_cast<long long>(first + g) * width + w] =
+        rows[static_cast<long long>(owner[g]) * width + w];
+  }
+}
+
+template <typename S>
+__global__ void k_reverse_self(S *rows, int width, const int *owner, int first, int n)
+{
+  const long long total = static_cast<long long>(n) * width;
+  for (long long flat = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; flat < total;
+       flat += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(flat / width), w = static_cast<int>(flat % width);
+    S *src = rows + static_cast<long long>(first + g) * width + w;
+    // Several images can share one owner, so the add is atomic.
+    atomicAdd(rows + static_cast<long long>(owner[g]) * width + w, *src);
+    *src = S(0);
+  }
+}
+
+}  // namespace ljx

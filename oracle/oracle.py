@@ -338,3 +338,50 @@ def eam_step(tables, x, types, nlocal, owner, list_, *, mode, precision="float64
         np.add.at(f, np.asarray(owner[:nghost]), f[nlocal:nall])
     return StepResult(f[:nlocal].copy(), f_all, scale * out.energy, virial, out.rho, out.fp,
                       count, overflow, senders, receivers, mask)
+
+
+def lj_step(x, nlocal, owner, list_, *, epsilon, sigma, cutoff, force_output="edge-force",
+            newton_pair=False, precision="float64", max_atoms=None, max_edges=None, scale=1.0,
+            pair_sum=False):
+    """One pair-style compute for an LJ bundle (examples/export_model.py + pair_jax_kokkos.cpp).
+
+    Edge-force bundles add dU/drij to the sender and, with newton on, subtract it from the
+    receiver (AddEdgeForcesFunctor, :195-225); atom-force bundles add the autodiff forces of the
+    0.5-per-edge energy over all rows (AddForcesFunctor, newton on). The per-edge energy scale
+    follows export_lj (:107). Newton-on runs take the f.r virial over all rows, then fold ghost
+    forces into owners; newton-off runs report the per-edge virial.
+    """
+    dtype = np.float64 if precision == "float64" else np.float32
+    nall = x.shape[0]
+    nghost = nall - nlocal
+    max_atoms = max_atoms or nall
+    ilist, numneigh, neighbors, stride, maxneigh = list_
+    edge = force_output == "edge-force"
+    duplicate = bool(newton_pair and pair_sum and not edge)
+    if max_edges is None:
+        max_edges = 2 * int(numneigh[:nlocal].sum()) + 1
+    senders, receivers, mask, count, overflow = pack_edges(
+        x, ilist, numneigh, neighbors, 1, stride, nlocal, maxneigh, max_atoms, max_edges, cutoff,
+        duplicate_reverse_edges=duplicate, nlocal=nlocal)
+    positions = np.zeros((max_atoms, 3), dtype)
+    positions[:nall] = x.astype(dtype)
+    escale = 1.0 if (edge and newton_pair) else 0.5
+    atom_energy, edge_force, model_force, energy, virial_edge = lj_model(
+        epsilon, sigma, cutoff, escale, positions, nlocal, nghost, senders, receivers, mask,
+        1.0 if newton_pair else 0.5, dtype=dtype)
+    f = np.zeros((nall, 3))
+    if edge:
+        c = min(count, max_edges)
+        fe = scale * edge_force[:c].astype(np.float64)
+        np.add.at(f, senders[:c], fe)
+        if newton_pair:
+            np.add.at(f, receivers[:c], -fe)
+    else:
+        rows = nall if newton_pair else nlocal
+        f[:rows] += scale * model_force[:rows].astype(np.float64)
+    virial = virial_fdotr(x, f) if newton_pair else scale * virial_edge
+    f_all = f.copy()
+    if newton_pair:
+        np.add.at(f, np.asarray(owner[:nghost]), f[nlocal:nall])
+    return StepResult(f[:nlocal].copy(), f_all, scale * energy, virial, None, None, count,
+                      overflow, senders, receivers, mask)
