@@ -1,0 +1,426 @@
+"""Benchmark: EAM force + energy + virial throughput (atom-steps/s) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ljx|reference] [--precision P]
+
+A step is one pair-style compute of the hot path on resident inputs: stage positions (a1),
+fused list filter/compaction + EAM density (a2+a6), embedding (a8), forward exchange of F'(rho)
+to the ghost images (a15), fused force/energy/virial (a9-a13), and the energy/virial readback.
+Workload at N=1: the 2,048,000-atom Cu fcc configuration (80^3 cells, a = 3.615 A, Gaussian
+jitter 0.08 A, synthetic EAM, rc 6.5 A, skin 2.0 A), float64, full list with newton off.
+The neighbor list is built once and held fixed (positions are static across timed steps); the
+list alone (about 1.9 GB) is larger than the 126 MB L2, so no separate flush is needed.
+
+--impl reference times the CPU restatement of the reference's path (oracle/, OpenMP on all host
+threads) on a bounded sample of the same workload (a 40^3-cell replica) and prints the same line
+with "impl": "reference".
+
+Multi-GPU runs (torchrun, one rank per GPU) use spatial decomposition along z: every rank owns a
+2,048,000-atom slab of a larger crystal (weak scaling) and exchanges F'(rho) of its boundary
+atoms with its two z-neighbors over NCCL each step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "EAM atom-steps/s (force+energy+virial)"
+UNIT = "atom-steps/s"
+CUTOFF, SKIN, A_CU, JITTER = 6.5, 2.0, 3.615, 0.08
+
+
+def package():
+    name = "lammps_jax_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg_dir = ROOT / "lammps-jax_b200"
+    spec = importlib.util.spec_from_file_location(
+        name, pkg_dir / "__init__.py", submodule_search_locations=[str(pkg_dir)])
+    module = importlib.util.module_from_spec(spec)
+    sys.modules[name] = module
+    spec.loader.exec_module(module)
+    return module
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def workload(cells, seed=2024):
+    ljx = package()
+    atoms = ljx.synth.fcc(cells, A_CU, jitter=JITTER, seed=seed)
+    x_all, owner = ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)
+    types_all = np.ones(len(x_all), np.int32)
+    return atoms, x_all, owner, types_all
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    def __init__(self, index: int, path: Path):
+        self.path = path
+        self.proc = None
+        self.index = index
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def profile_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if present."""
+    path = ROOT / "profiles" / "dram_traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+def run_ljx(args):
+    import torch
+    import torch.distributed as dist
+
+    ljx = package()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    cells = (80, 80, 80)
+    precision = args.precision
+    if world > 1:
+        system, nlocal, nall, decomp = setup_decomposed(ljx, cells, rank, world, precision, local)
+    else:
+        system, nlocal, nall, decomp = setup_single(ljx, cells, precision)
+    pair = decomp["pair"]
+    stream = torch.cuda.current_stream()
+    eng = pair.engine
+    atoms = system.atoms()
+    nl = system.list.struct()
+    fp_rows, width, elem = eng.feature_rows(1)
+
+    names = ["pack_atoms", "density", "embed", "halo_fp", "force", "result"]
+
+    def step(events=None):
+        def mark(k):
+            if events is not None:
+                events[k].record(stream)
+        mark(0)
+        eng.pack_atoms(atoms)
+        mark(1)
+        eng.density(atoms, nl, False)
+        mark(2)
+        eng.embed(atoms)
+        mark(3)
+        system.comm.forward(fp_rows, width, elem)
+        mark(4)
+        eng.force(atoms, nl, False, 1.0)
+        mark(5)
+        res = eng.read_result()
+        mark(6)
+        return res
+
+    system.f.zero_()
+    for _ in range(args.warmup):
+        res = step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches0 = eng.launches
+    kevents = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv") as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start.record(stream)
+        for k in range(args.steps):
+            res = step(kevents[k])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    elapsed = start.elapsed_time(stop) / 1e3
+    if world > 1:
+        t = torch.tensor([elapsed], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    # Our kernels per step: pack_atoms, density, embed, forward exchange, force, finalize.
+    launches = (eng.launches - launches0) + args.steps * decomp["comm_launches"]
+    phase = {n: 0.0 for n in names}
+    for ev in kevents:
+        for k, n in enumerate(names):
+            phase[n] += ev[k].elapsed_time(ev[k + 1]) / 1e3
+    phase = {n: v / args.steps for n, v in phase.items()}
+
+    # Algorithmic bytes per launch (per step) of the two row kernels.
+    nn = system.list.numneigh[:nlocal].to(torch.int64)
+    listed = int(nn.sum().item())
+    kept = int(res.edge_count)
+    real = 8 if precision == "float64" else 4
+    bytes_density = 4 * listed + 4 * nlocal * 2 + 32 * nall + 4 * kept + 4 * nlocal + real * nlocal
+    pos_bytes = 32 if precision == "float64" else 16
+    bytes_force = 8 * nlocal + 4 * kept + pos_bytes * nall + real * nall + 48 * nlocal
+    kernel = max(("density", "force"), key=lambda n: phase[n])
+    kbytes = bytes_density if kernel == "density" else bytes_force
+    achieved = kbytes / phase[kernel] / 1e9
+    peak, peak_kind = peaks()
+    kname = {"density": f"k_density_full_{precision}", "force": f"k_force_rows_full_{precision}"}[kernel]
+    traffic = profile_traffic(kname)
+
+    e2e = run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall, world)
+    value = world * nlocal * args.steps / elapsed
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f64" if precision == "float64" else "f32", "data": "synthetic",
+        "config": {
+            "workload": "C3: Cu fcc 80^3 cells (2,048,000 atoms) per GPU, synthetic EAM "
+                        "rc 6.5 A skin 2.0 A, full list, newton off, forward F'(rho) exchange",
+            "atoms_per_gpu": nlocal, "ghosts_per_gpu": nall - nlocal,
+            "listed_pairs_per_atom": listed / nlocal, "kept_edges_per_atom": kept / nlocal,
+            "precision": precision, "l2": "inputs larger than L2 (neighbor list "
+                                           f"{system.list.neighbors.numel() * 4 / 1e9:.2f} GB)",
+            "list": "built once on the device, fixed over timed steps",
+            "parallelism": decomp["parallelism"],
+            "phase_ms": {n: v * 1e3 for n, v in phase.items()},
+        },
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "algorithmic_bytes": kbytes, "traffic": traffic},
+        "gpu_launches": launches,
+        "e2e": e2e,
+        "energy_per_atom": res.energy / nlocal,
+    }
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(args)
+    clocks_summary = clocks.summary()
+    line["clocks"] = clocks_summary
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    pair.engine.close()
+    if world > 1:
+        decomp["close"]()
+        dist.destroy_process_group()
+
+
+def setup_single(ljx, cells, precision):
+    import tempfile
+
+    import torch
+    atoms, x_all, owner, types_all = workload(cells)
+    nlocal, nall = len(atoms.x), len(x_all)
+    text = ljx.synth.synthetic_setfl(("Cu",))
+    tmp = Path(tempfile.mkdtemp())
+    path = tmp / "c3.json"
+    max_atoms = nall + 1024
+    ljx.write_bundle(path, potential=ljx.eam_potential(text), max_atoms=max_atoms,
+                     max_edges=max_atoms * 128, cutoff=CUTOFF, unit_style="metal",
+                     precision=precision, force_output="atom-force", newton="off", comm=True,
+                     n_species=1)
+    x = torch.as_tensor(x_all, device="cuda")
+    system = ljx.System(x=x, type=torch.as_tensor(types_all, device="cuda"),
+                        f=torch.zeros_like(x), nlocal=nlocal, nghost=nall - nlocal,
+                        newton_pair=False, unit_style="metal", ntypes=1)
+    pair = ljx.PairJax()
+    pair.coeff(system, "*", "*", str(path))
+    pair.init_style(system)
+    system.list = ljx.synth.neighbor_list(x_all, nlocal, CUTOFF + SKIN, half=False)
+    system.comm = ljx.SelfComm(torch.as_tensor(owner, device="cuda"), nlocal)
+    return system, nlocal, nall, {"pair": pair, "parallelism": "single GPU (periodic self-images)",
+                                  "comm_launches": 1}
+
+
+def setup_decomposed(ljx, cells, rank, world, precision, local):
+    raise SystemExit("multi-GPU spatial decomposition is not wired into bench.py yet")
+
+
+def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall, world):
+    """Same step through the C ABI with host buffers: H2D of x every step and of the neighbor
+    list every 10th step (the C3 rebuild period), D2H of forces and the result every step."""
+    x_host = system.x.cpu().pin_memory()
+    f_host = torch.empty_like(system.f, device="cpu").pin_memory()
+    nb = system.list.neighbors
+    nb_host = nb.cpu().pin_memory()
+    nn_host = system.list.numneigh.cpu().pin_memory()
+    stream = torch.cuda.current_stream()
+    steps = max(3, min(args.steps, 10))
+
+    def one(k):
+        system.x.copy_(x_host, non_blocking=True)
+        h2d = x_host.numel() * 8
+        if k % 10 == 0:
+            nb.copy_(nb_host, non_blocking=True)
+            system.list.numneigh.copy_(nn_host, non_blocking=True)
+            h2d += nb_host.numel() * 4 + nn_host.numel() * 4
+        eng.pack_atoms(atoms)
+        eng.density(atoms, nl, False)
+        eng.embed(atoms)
+        system.comm.forward(fp_rows, width, elem)
+        eng.force(atoms, nl, False, 1.0)
+        f_host.copy_(system.f, non_blocking=True)
+        eng.read_result()  # synchronizes the stream: forces and energy are on the host
+        return h2d
+
+    one(1)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    h2d = 0
+    for k in range(steps):
+        h2d += one(k)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    elapsed = start.elapsed_time(stop) / 1e3
+    del t0
+    value = world * system.nlocal * steps / elapsed
+    return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d / steps,
+            "d2h_bytes_per_step": f_host.numel() * 8 + 9 * 8, "steps": steps}
+
+
+def cpu_baseline(args, sample_cells=(40, 40, 40), steps=None):
+    """The CPU restatement (oracle, all host threads) on a bounded replica of the workload."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    oracle.lib()
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    ljx = package()
+    atoms, x_all, owner, types_all = workload(sample_cells, seed=7)
+    nlocal = len(atoms.x)
+    tables = oracle.parse_setfl_text(ljx.synth.synthetic_setfl(("Cu",)))
+    lst = oracle.build_list(x_all, nlocal, CUTOFF + SKIN, half=False)
+    oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
+                    precision=args.precision)
+    steps = steps or 2
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
+                        precision=args.precision)
+    dt = time.perf_counter() - t0
+    return {"value": nlocal * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{sample_cells[0]}^3-cell replica of the workload ({nlocal} atoms), "
+                      f"{steps} full steps (pack + density + embedding + exchange + forces + "
+                      "virial), oracle/eam_oracle.c with OpenMP"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    oracle.lib()
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    ljx = package()
+    cells = (40, 40, 40)
+    atoms, x_all, owner, types_all = workload(cells, seed=7)
+    nlocal = len(atoms.x)
+    tables = oracle.parse_setfl_text(ljx.synth.synthetic_setfl(("Cu",)))
+    lst = oracle.build_list(x_all, nlocal, CUTOFF + SKIN, half=False)
+    steps = max(1, min(args.steps, 5))
+    for _ in range(min(args.warmup, 1)):
+        oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
+                        precision=args.precision)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
+                        precision=args.precision)
+    dt = time.perf_counter() - t0
+    value = nlocal * steps / dt
+    sample = (f"40^3-cell replica of the C3 workload ({nlocal} atoms, same lattice, potential, "
+              f"cutoffs and list), {steps} timed steps")
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": dt / steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f64" if args.precision == "float64" else "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "C3: Cu fcc, synthetic EAM rc 6.5 A skin 2.0 A, full list, "
+                               "newton off (CPU sample)", "precision": args.precision},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own CPU path (LAMMPS Kokkos-OpenMP + XLA CPU PJRT) is not "
+                "installable offline; this times the CPU restatement of that path",
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ljx", "reference"), default="ljx")
+    ap.add_argument("--precision", choices=("float64", "float32"), default="float64")
+    args = ap.parse_args()
+    (ROOT / "gpurun_out").mkdir(exist_ok=True)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ljx(args)
+
+
+if __name__ == "__main__":
+    main()

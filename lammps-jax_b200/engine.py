@@ -11,6 +11,7 @@ neighbor list) and `SelfComm` for LAMMPS's comm on one rank whose ghosts are per
 
 from __future__ import annotations
 
+import builtins
 import ctypes
 from dataclasses import dataclass, field
 
@@ -65,7 +66,7 @@ class System:
     ntypes: int = 1
     list: NeighborList | None = None
     comm: object = None
-    fixes: list = field(default_factory=list)
+    fixes: builtins.list = field(default_factory=builtins.list)
 
     @property
     def nall(self) -> int:
