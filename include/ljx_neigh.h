@@ -6,6 +6,7 @@
  *
  * Binning: atoms are pre-sorted into a uniform grid of cubic bins (side `binsize` >= cutoff/2,
  * origin `lo`, `nbins` per dimension); bin b holds bin_atoms[bin_start[b] .. bin_start[b+1]).
+ * `lo` (3 doubles) and `nbins` (3 ints) are HOST arrays; every other pointer is device memory.
  * Each owned atom scans a +-2 bin stencil. half != 0 keeps each pair once: owned j > i, or a
  * ghost j whose (z, y, x) sorts after atom i's — the one-rank-per-pair rule of the reference
  * packer (cpp/pair_jax_kokkos.cpp:94-101).

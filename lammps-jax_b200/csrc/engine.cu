@@ -251,6 +251,7 @@ ljx::Step<T> make_step(ljx_engine *e, const ljx_atoms *a, const ljx_list *l, dou
   p.embedding = static_cast<const V *>(e->embedding);
   p.density = static_cast<const V *>(e->density);
   p.pair = static_cast<const V *>(e->pair);
+  p.n_species = e->c.potential == LJX_POTENTIAL_EAM ? std::max(1, e->bundle.eam.n_elements) : 1;
   p.nrho = e->bundle.eam.nrho;
   p.nr = e->bundle.eam.nr;
   p.drho = static_cast<T>(e->bundle.eam.drho);

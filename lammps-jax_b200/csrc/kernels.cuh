@@ -68,6 +68,7 @@ struct Step {
   const typename Vec4<T>::type *embedding;
   const typename Vec4<T>::type *density;
   const typename Vec4<T>::type *pair;
+  int n_species;                      // table count; species clamp to [0, n_species)
   int nrho;
   int nr;
   T drho;
@@ -201,7 +202,8 @@ __global__ void __launch_bounds__(kBlock) k_pack_atoms(const Step<T> p, int span
 {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < span; i += gridDim.x * blockDim.x) {
     const double x0 = p.x[3 * i], x1 = p.x[3 * i + 1], x2 = p.x[3 * i + 2];
-    const int s = p.type[i] - 1;
+    // Types past the table map to the last species (the clamped gather of the reference model).
+    const int s = min(max(p.type[i] - 1, 0), p.n_species - 1);
     p.xd4[i] = make_double4(x0, x1, x2, static_cast<double>(s));
     if (p.pos4 != nullptr) {
       reinterpret_cast<float4 *>(p.pos4)[i] =
@@ -292,7 +294,7 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
   const T inv_drho = T(1) / p.drho;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.nlocal;
        i += gridDim.x * blockDim.x) {
-    const int s = p.type[i] - 1;
+    const int s = min(max(p.type[i] - 1, 0), p.n_species - 1);
     const T rho = p.rho[i];
     const T idx = rho / p.drho;
     T fl = floor(idx);
@@ -356,7 +358,7 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   v[3] -= w * static_cast<double>(dx * ey);
   v[4] -= w * static_cast<double>(dx * ez);
   v[5] -= w * static_cast<double>(dy * ez);
-  if (MODE != kRowsFull) {
+  if (MODE != kRowsFull && j < p.nall) {
     atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
     atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
     atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
     fx = warp_sum(fx);
     fy = warp_sum(fy);
     fz = warp_sum(fz);
-    if (lane == 0) {
+    if (lane == 0 && i < p.nall) {
       double *fi = p.f + 3 * i;
       if (MODE == kRowsFull) {
         fi[0] += p.scale * static_cast<double>(fx);
@@ -480,7 +482,7 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
       v[3] -= vw * static_cast<double>(dx * ey);
       v[4] -= vw * static_cast<double>(dx * ez);
       v[5] -= vw * static_cast<double>(dy * ez);
-      if (scatter) {
+      if (scatter && j < p.nall) {
         atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
         atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
         atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
@@ -489,7 +491,7 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
     fx = warp_sum(fx);
     fy = warp_sum(fy);
     fz = warp_sum(fz);
-    if (lane == 0) {
+    if (lane == 0 && i < p.nall) {
       double *fi = p.f + 3 * i;
       if (!scatter) {
         fi[0] += p.scale * static_cast<double>(fx);
