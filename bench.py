@@ -144,7 +144,7 @@ def run_ljx(args):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    cells = (80, 80, 80)
+    cells = (args.cells, args.cells, args.cells)
     precision = args.precision
     if world > 1:
         system, nlocal, nall, decomp = setup_decomposed(ljx, cells, rank, world, precision, local)
@@ -224,7 +224,8 @@ def run_ljx(args):
     kname = {"density": f"k_density_full_{precision}", "force": f"k_force_rows_full_{precision}"}[kernel]
     traffic = profile_traffic(kname)
 
-    e2e = run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall, world)
+    e2e = None if args.skip_extras else run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows,
+                                                 width, elem, args, nall, world)
     value = world * nlocal * args.steps / elapsed
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -232,8 +233,8 @@ def run_ljx(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f64" if precision == "float64" else "f32", "data": "synthetic",
         "config": {
-            "workload": "C3: Cu fcc 80^3 cells (2,048,000 atoms) per GPU, synthetic EAM "
-                        "rc 6.5 A skin 2.0 A, full list, newton off, forward F'(rho) exchange",
+            "workload": f"C3: Cu fcc {args.cells}^3 cells ({nlocal:,} atoms) per GPU, synthetic "
+                        "EAM rc 6.5 A skin 2.0 A, full list, newton off, forward F'(rho) exchange",
             "atoms_per_gpu": nlocal, "ghosts_per_gpu": nall - nlocal,
             "listed_pairs_per_atom": listed / nlocal, "kept_edges_per_atom": kept / nlocal,
             "precision": precision, "l2": "inputs larger than L2 (neighbor list "
@@ -249,7 +250,7 @@ def run_ljx(args):
         "e2e": e2e,
         "energy_per_atom": res.energy / nlocal,
     }
-    if world == 1:
+    if world == 1 and not args.skip_extras:
         line["cpu_baseline"] = cpu_baseline(args)
     clocks_summary = clocks.summary()
     line["clocks"] = clocks_summary
@@ -414,6 +415,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ljx", "reference"), default="ljx")
     ap.add_argument("--precision", choices=("float64", "float32"), default="float64")
+    ap.add_argument("--cells", type=int, default=80,
+                    help="fcc cells per edge of each rank's box (80 = the 2,048,000-atom config)")
+    ap.add_argument("--skip-extras", action="store_true",
+                    help="time the device path only (no e2e or CPU-baseline legs); for profiling")
     args = ap.parse_args()
     (ROOT / "gpurun_out").mkdir(exist_ok=True)
     if args.impl == "reference":
