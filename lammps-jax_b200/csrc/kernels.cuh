@@ -17,6 +17,10 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kNeighMask = 0x1FFFFFFF;
 // One block's partial sums: [0] energy, [1..6] virial, [7] kept pairs, [8] widest row (max).
 constexpr int kPartialWidth = 10;
+// List slots of one row staged in shared memory per block row-group (longer rows read the rest
+// straight from global memory), and the per-warp queue of kept pairs.
+constexpr int kTileSlots = 384;
+constexpr int kQueue = 64;
 
 enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2 };
 // Force distribution modes.
@@ -31,11 +35,15 @@ template <typename T> struct Vec4;
 template <> struct Vec4<float> { using type = float4; };
 template <> struct Vec4<double> { using type = double4; };
 
+// One 32-byte record per lane in a single request (sm_100 256-bit vector load through the
+// read-only path). Only used on data no kernel writes while the reading kernel runs.
 __device__ __forceinline__ double4 load4(const double4 *p)
 {
-  const double2 a = __ldg(reinterpret_cast<const double2 *>(p));
-  const double2 b = __ldg(reinterpret_cast<const double2 *>(p) + 1);
-  return make_double4(a.x, a.y, b.x, b.y);
+  double4 v;
+  asm("ld.global.nc.v4.f64 {%0, %1, %2, %3}, [%4];"
+      : "=d"(v.x), "=d"(v.y), "=d"(v.z), "=d"(v.w)
+      : "l"(p));
+  return v;
 }
 __device__ __forceinline__ float4 load4(const float4 *p) { return __ldg(p); }
 
@@ -214,71 +222,157 @@ __global__ void __launch_bounds__(kBlock) k_pack_atoms(const Step<T> p, int span
 }
 
 // a2 + a6: filter and compact each list row, accumulating the EAM density.
-// partials[block] = {kept pairs, widest row, ...}.
+//
+// A block takes 8 consecutive list rows at a time (one per warp). The rows' list slots are first
+// staged in shared memory: with the Kokkos LayoutLeft list, slot s of 8 consecutive rows is one
+// 32-byte sector, so the staging load is coalesced where a warp walking one row directly would
+// touch a different cache line per lane. Each warp then filters its row 32 slots at a time
+// (reference distance test and pairing rules), and a ballot appends the kept pairs to a
+// per-warp queue in shared memory; every 32 queued pairs are written out as one coalesced
+// segment of the compacted row and evaluated by all 32 lanes together (sqrt + density spline),
+// so the floating-point work runs at full lane occupancy instead of at the ~40% keep rate.
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
 {
+  __shared__ int s_tile[kTileSlots][kWarpsPerBlock + 1];
+  __shared__ int s_row_i[kWarpsPerBlock];
+  __shared__ int s_row_n[kWarpsPerBlock];
+  __shared__ int s_qj[kWarpsPerBlock][kQueue];
+  __shared__ T s_qr2[kWarpsPerBlock][kQueue];
+  __shared__ unsigned char s_qs[kWarpsPerBlock][kQueue];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
+  int *qj = s_qj[warp];
+  T *qr2 = s_qr2[warp];
+  unsigned char *qs = s_qs[warp];
   double kept_sum = 0.0;
   int widest = 0;
-  for (int row = blockIdx.x * kWarpsPerBlock + warp; row < p.inum;
-       row += gridDim.x * kWarpsPerBlock) {
-    const int i = p.ilist[row];
-    if (i >= p.max_atoms) {
-      if (lane == 0) p.ccount[row] = 0;
-      continue;
-    }
-    const int listed = p.numneigh[i];
-    widest = max(widest, listed);
-    const int n = min(listed, p.maxneighs);
-    const double4 xi = load4(p.xd4 + i);
-    const int si = static_cast<int>(xi.w);
-    int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
-    const long long rowbase = static_cast<long long>(i) * p.atom_stride;
-    T rho = T(0);
-    int kept = 0;
-    for (int base = 0; base < n; base += kWarp) {
-      const int jj = base + lane;
-      int j = 0;
-      bool keep = false;
-      double4 xj = make_double4(0, 0, 0, 0);
-      if (jj < n) {
-        j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
-        if (j < p.max_atoms) {
-          xj = load4(p.xd4 + j);
-          keep = pack_keep(p, i, xi, j, xj);
+  const int groups = (p.inum + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  const bool slot_major = p.atom_stride == 1;
+  for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+    const int row0 = g * kWarpsPerBlock;
+    if (threadIdx.x < kWarpsPerBlock) {
+      const int row = row0 + threadIdx.x;
+      int i = -1, n = 0;
+      if (row < p.inum) {
+        i = p.ilist[row];
+        if (i < p.max_atoms) {
+          const int listed = p.numneigh[i];
+          widest = max(widest, listed);
+          n = min(listed, p.maxneighs);
+        } else {
+          i = -1;
         }
       }
-      const unsigned m = __ballot_sync(kFull, keep);
-      if (keep) {
-        const int slot = kept + __popc(m & below);
-        if (slot < p.row_cap) crow[slot] = j;
-        if (MODE != kCompactOnly) {
-          const T dx = T(xj.x) - T(xi.x), dy = T(xj.y) - T(xi.y), dz = T(xj.z) - T(xi.z);
-          const T r2 = dx * dx + dy * dy + dz * dz;
-          if (r2 < p.model_cutsq) {
+      s_row_i[threadIdx.x] = i;
+      s_row_n[threadIdx.x] = n;
+    }
+    __syncthreads();
+    int wmax = 0;
+#pragma unroll
+    for (int r = 0; r < kWarpsPerBlock; ++r) wmax = max(wmax, min(s_row_n[r], kTileSlots));
+    for (int t = threadIdx.x; t < wmax * kWarpsPerBlock; t += kBlock) {
+      const int r = slot_major ? t % kWarpsPerBlock : t / wmax;
+      const int sl = slot_major ? t / kWarpsPerBlock : t % wmax;
+      const int ii = s_row_i[r];
+      if (ii >= 0 && sl < s_row_n[r])
+        s_tile[sl][r] = p.neighbors[static_cast<long long>(ii) * p.atom_stride +
+                                    static_cast<long long>(sl) * p.slot_stride] & kNeighMask;
+    }
+    __syncthreads();
+    const int row = row0 + warp;
+    const int i = s_row_i[warp];
+    const int n = s_row_n[warp];
+    if (row < p.inum && i < 0 && lane == 0) p.ccount[row] = 0;
+    if (row < p.inum && i >= 0) {
+      const double4 xi = load4(p.xd4 + i);
+      const int si = static_cast<int>(xi.w);
+      int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
+      const long long rowbase = static_cast<long long>(i) * p.atom_stride;
+      T rho = T(0);
+      int kept = 0;  // pairs already written out
+      int q = 0;     // pairs waiting in the queue
+      // Write out and evaluate the first `count` queued pairs (count <= 32), then drop them.
+      auto flush = [&](int count) {
+        __syncwarp();
+        int j = 0, sj = 0;
+        T r2 = T(0);
+        if (lane < count) {
+          j = qj[lane];
+          r2 = qr2[lane];
+          sj = qs[lane];
+        }
+        int tj = 0, ts = 0;
+        T tr2 = T(0);
+        const int rest = q - count;
+        if (lane < rest) {
+          tj = qj[count + lane];
+          tr2 = qr2[count + lane];
+          ts = qs[count + lane];
+        }
+        __syncwarp();
+        if (lane < rest) {
+          qj[lane] = tj;
+          qr2[lane] = tr2;
+          qs[lane] = static_cast<unsigned char>(ts);
+        }
+        __syncwarp();
+        if (lane < count) {
+          const int slot = kept + lane;
+          if (slot < p.row_cap) crow[slot] = j;
+          if (MODE != kCompactOnly && r2 < p.model_cutsq) {
             const T r = sqrt(r2);
-            const int sj = static_cast<int>(xj.w);
             rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
             if (MODE == kDensityHalf)
               atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
           }
         }
+        kept += count;
+        q = rest;
+      };
+      for (int base = 0; base < n; base += kWarp) {
+        const int jj = base + lane;
+        int j = 0, sj = 0;
+        bool keep = false;
+        T r2m = T(0);
+        if (jj < n) {
+          j = jj < kTileSlots ? s_tile[jj][warp]
+                              : (p.neighbors[rowbase + static_cast<long long>(jj) * p.slot_stride] &
+                                 kNeighMask);
+          if (j < p.max_atoms) {
+            const double4 xj = load4(p.xd4 + j);
+            keep = pack_keep(p, i, xi, j, xj);
+            if (keep) {
+              const T dx = T(xj.x) - T(xi.x), dy = T(xj.y) - T(xi.y), dz = T(xj.z) - T(xi.z);
+              r2m = dx * dx + dy * dy + dz * dz;
+              sj = static_cast<int>(xj.w);
+            }
+          }
+        }
+        const unsigned m = __ballot_sync(kFull, keep);
+        if (keep) {
+          const int at = q + __popc(m & below);
+          qj[at] = j;
+          qr2[at] = r2m;
+          qs[at] = static_cast<unsigned char>(sj);
+        }
+        q += __popc(m);
+        if (q >= kWarp) flush(kWarp);
       }
-      kept += __popc(m);
-    }
-    if (MODE != kCompactOnly) {
-      rho = warp_sum(rho);
-      if (lane == 0) {
-        if (MODE == kDensityHalf)
-          atomicAdd(p.rho + i, rho);
-        else
-          p.rho[i] = rho;
+      if (q > 0) flush(q);
+      if (MODE != kCompactOnly) {
+        rho = warp_sum(rho);
+        if (lane == 0) {
+          if (MODE == kDensityHalf)
+            atomicAdd(p.rho + i, rho);
+          else
+            p.rho[i] = rho;
+        }
       }
+      if (lane == 0) p.ccount[row] = kept;
+      kept_sum += kept;
     }
-    if (lane == 0) p.ccount[row] = kept;
-    kept_sum += kept;
+    __syncthreads();
   }
   // kept_sum is carried by lane 0 of each warp (the other lanes hold copies): count it once.
   double acc[8] = {0, 0, 0, 0, 0, 0, 0, lane == 0 ? kept_sum : 0.0};

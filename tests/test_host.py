@@ -22,11 +22,14 @@ def test_fcc_and_ghost_images(ljx):
     assert set(np.unique(owner)) == set(np.nonzero(near)[0])
 
 
-def test_brick_order_is_spatially_compact(ljx):
-    atoms = ljx.synth.fcc((8, 8, 8), 3.615, seed=0, brick=4)
-    first = atoms.x[:256]  # one brick of 4^3 cells
-    span = first.max(0) - first.min(0)
-    assert np.all(span < 4 * 3.615)
+def test_lammps_sort_order(ljx):
+    atoms = ljx.synth.fcc((8, 8, 8), 3.615, seed=0, sort_binsize=4.25)
+    nb = np.floor(atoms.box / 4.25).astype(int)
+    c = np.floor(atoms.x / (atoms.box / nb)).astype(int)
+    ibin = (c[:, 2] * nb[1] + c[:, 1]) * nb[0] + c[:, 0]
+    assert np.all(np.diff(ibin) >= 0)  # bin index non-decreasing, x fastest
+    plain = ljx.synth.fcc((8, 8, 8), 3.615, seed=0, sort_binsize=None)
+    assert sorted(map(tuple, np.round(plain.x, 9))) == sorted(map(tuple, np.round(atoms.x, 9)))
 
 
 def test_substitutional_counts(ljx):
