@@ -73,7 +73,9 @@ struct ljx_engine {
   int *ccount = nullptr;
   void *embedding = nullptr;
   void *density = nullptr;
+  void *density_slope = nullptr;
   void *pair = nullptr;
+  unsigned int *coord_bound = nullptr;
   int *senders = nullptr;
   int *receivers = nullptr;
   uint8_t *edge_mask = nullptr;
@@ -94,9 +96,9 @@ struct ljx_engine {
   ~ljx_engine()
   {
     cudaSetDevice(device);
-    void *ptrs[] = {xd4,     pos4,      rho,       fp,      cedges,     ccount,
-                    embedding, density, pair,      senders, receivers,  edge_mask,
-                    offsets, count_prev, partials, result};
+    void *ptrs[] = {xd4,       pos4,      rho,        fp,          cedges,  ccount,
+                    embedding, density,   density_slope, pair,     coord_bound, senders,
+                    receivers, edge_mask, offsets,    count_prev,  partials, result};
     for (void *p : ptrs)
       if (p) cudaFree(p);
     if (host_result) cudaFreeHost(host_result);
@@ -250,7 +252,9 @@ ljx::Step<T> make_step(ljx_engine *e, const ljx_atoms *a, const ljx_list *l, dou
   p.row_cap = e->row_cap;
   p.embedding = static_cast<const V *>(e->embedding);
   p.density = static_cast<const V *>(e->density);
+  p.density_slope = static_cast<const V *>(e->density_slope);
   p.pair = static_cast<const V *>(e->pair);
+  p.coord_bound = e->coord_bound;
   p.n_species = e->c.potential == LJX_POTENTIAL_EAM ? std::max(1, e->bundle.eam.n_elements) : 1;
   p.nrho = e->bundle.eam.nrho;
   p.nr = e->bundle.eam.nr;
@@ -486,6 +490,7 @@ ljx_status pack_atoms_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a)
 {
   ljx::Step<T> p = make_step<T>(e, a, nullptr, 1.0);
   const int span = std::min(p.nall, e->c.max_atoms);
+  check(cudaMemsetAsync(e->coord_bound, 0, sizeof(unsigned int), s), "cudaMemsetAsync(bound)");
   if (span <= 0) return LJX_OK;
   ljx::k_pack_atoms<T><<<flat_grid(span), ljx::kBlock, 0, s>>>(p, span);
   check_launch("k_pack_atoms");
@@ -599,10 +604,11 @@ ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **
     e->max_grid = e->sm_count * 8;
     e->xd4 = static_cast<double4 *>(device_alloc(max_atoms * sizeof(double4), "cudaMalloc(xd4)"));
     check(cudaMemset(e->xd4, 0, max_atoms * sizeof(double4)), "cudaMemset(xd4)");
-    if (!e->f64) {
-      e->pos4 = device_alloc(max_atoms * sizeof(float4), "cudaMalloc(pos4)");
-      check(cudaMemset(e->pos4, 0, max_atoms * sizeof(float4)), "cudaMemset(pos4)");
-    }
+    // Float copy of the positions: the distance pre-filter (and the float model) reads it.
+    e->pos4 = device_alloc(max_atoms * sizeof(float4), "cudaMalloc(pos4)");
+    check(cudaMemset(e->pos4, 0, max_atoms * sizeof(float4)), "cudaMemset(pos4)");
+    e->coord_bound = static_cast<unsigned int *>(device_alloc(sizeof(unsigned int), "cudaMalloc(bound)"));
+    check(cudaMemset(e->coord_bound, 0, sizeof(unsigned int)), "cudaMemset(bound)");
     e->rho = device_alloc(max_atoms * real, "cudaMalloc(rho)");
     e->fp = device_alloc(max_atoms * real, "cudaMalloc(fp)");
     check(cudaMemset(e->rho, 0, max_atoms * real), "cudaMemset(rho)");
@@ -642,13 +648,24 @@ ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **
           "cudaMallocHost(result)");
     if (c.potential == LJX_POTENTIAL_EAM) {
       const ljx::EamTables &t = e->bundle.eam;
+      // Slope rows (c1, 2 c2, 3 c3, 0) / dr: d rho/dr = s0 + t (s1 + t s2).
+      std::vector<double> slope(t.density.size());
+      const double inv_dr = 1.0 / t.dr;
+      for (size_t k = 0; k < slope.size(); k += 4) {
+        slope[k + 0] = t.density[k + 1] * inv_dr;
+        slope[k + 1] = 2.0 * t.density[k + 2] * inv_dr;
+        slope[k + 2] = 3.0 * t.density[k + 3] * inv_dr;
+        slope[k + 3] = 0.0;
+      }
       if (e->f64) {
         e->embedding = upload_table<double>(t.embedding);
         e->density = upload_table<double>(t.density);
+        e->density_slope = upload_table<double>(slope);
         e->pair = upload_table<double>(t.pair);
       } else {
         e->embedding = upload_table<float>(t.embedding);
         e->density = upload_table<float>(t.density);
+        e->density_slope = upload_table<float>(slope);
         e->pair = upload_table<float>(t.pair);
       }
     }

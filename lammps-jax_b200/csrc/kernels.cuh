@@ -75,6 +75,7 @@ struct Step {
   // Tables: [n_el][n][4] at contract precision.
   const typename Vec4<T>::type *embedding;
   const typename Vec4<T>::type *density;
+  const typename Vec4<T>::type *density_slope;  // (c1, 2 c2, 3 c3, 0) / dr per node
   const typename Vec4<T>::type *pair;
   int n_species;                      // table count; species clamp to [0, n_species)
   int nrho;
@@ -93,6 +94,8 @@ struct Step {
   T lj_four_eps;
   T lj_sigma_sq;
   T lj_energy_scale;
+  // Largest |coordinate| of this step's atoms (float bits), for the float pre-filter bound.
+  unsigned int *coord_bound;
   // Per-block partial sums.
   double *partials;
 };
@@ -204,21 +207,49 @@ __device__ __forceinline__ bool pack_keep(const Step<T> &p, int i, const double4
   return true;
 }
 
-// a1: LAMMPS x/type -> xd4 (and the float copy): cpp/pair_jax_kokkos.cpp:35-52.
+// a1: LAMMPS x/type -> xd4 and its float copy (cpp/pair_jax_kokkos.cpp:35-52), plus the
+// largest |coordinate| (atomic max on float bits; *coord_bound is zeroed before the launch).
 template <typename T>
 __global__ void __launch_bounds__(kBlock) k_pack_atoms(const Step<T> p, int span)
 {
+  float big = 0.0f;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < span; i += gridDim.x * blockDim.x) {
     const double x0 = p.x[3 * i], x1 = p.x[3 * i + 1], x2 = p.x[3 * i + 2];
     // Types past the table map to the last species (the clamped gather of the reference model).
     const int s = min(max(p.type[i] - 1, 0), p.n_species - 1);
     p.xd4[i] = make_double4(x0, x1, x2, static_cast<double>(s));
-    if (p.pos4 != nullptr) {
-      reinterpret_cast<float4 *>(p.pos4)[i] =
-          make_float4(static_cast<float>(x0), static_cast<float>(x1), static_cast<float>(x2),
-                      static_cast<float>(s));
-    }
+    const float4 f = make_float4(static_cast<float>(x0), static_cast<float>(x1),
+                                 static_cast<float>(x2), static_cast<float>(s));
+    reinterpret_cast<float4 *>(p.pos4)[i] = f;
+    big = fmaxf(big, fmaxf(fabsf(f.x), fmaxf(fabsf(f.y), fabsf(f.z))));
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) big = fmaxf(big, __shfl_xor_sync(kFull, big, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(p.coord_bound, __float_as_uint(big));
+}
+
+// Band around rc^2 inside which a float r^2 cannot decide the reference's double test
+// r^2 <= rc^2. Float coordinates carry at most u|x| rounding (u = 2^-24, |x| <= X), so a float
+// difference is off by E <= 2uX' + u(R + 2uX') for |d| <= R, and the float r^2 by at most
+// 2 sqrt(3) R E + 3 E^2 + 4 u R^2 (three rounded products and two rounded sums). The band is
+// twice that plus 1e-6 R^2; pairs inside it take the exact double test.
+struct FilterBand {
+  float lo;  // float r^2 below: certainly kept
+  float hi;  // float r^2 above: certainly dropped
+};
+
+__device__ __forceinline__ FilterBand filter_band(double cutsq, unsigned int bound_bits)
+{
+  const double u = 5.9604644775390625e-8;
+  const double X = static_cast<double>(__uint_as_float(bound_bits)) * (1.0 + 4.0 * u);
+  const double R = sqrt(cutsq) + 1.0;
+  const double E = 2.0 * u * X + u * (R + 2.0 * u * X);
+  const double d = 2.0 * (2.0 * 1.7320508075688772 * R * E + 3.0 * E * E + 4.0 * u * R * R) +
+                   1e-6 * R * R;
+  FilterBand b;
+  b.lo = static_cast<float>(cutsq - d);
+  b.hi = static_cast<float>(cutsq + d);
+  return b;
 }
 
 // a2 + a6: filter and compact each list row, accumulating the EAM density.
@@ -238,17 +269,18 @@ __global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
   __shared__ int s_row_i[kWarpsPerBlock];
   __shared__ int s_row_n[kWarpsPerBlock];
   __shared__ int s_qj[kWarpsPerBlock][kQueue];
-  __shared__ T s_qr2[kWarpsPerBlock][kQueue];
-  __shared__ unsigned char s_qs[kWarpsPerBlock][kQueue];
+  __shared__ float s_qr2[kWarpsPerBlock][kQueue];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
   int *qj = s_qj[warp];
-  T *qr2 = s_qr2[warp];
-  unsigned char *qs = s_qs[warp];
+  float *qr2 = s_qr2[warp];
   double kept_sum = 0.0;
   int widest = 0;
   const int groups = (p.inum + kWarpsPerBlock - 1) / kWarpsPerBlock;
   const bool slot_major = p.atom_stride == 1;
+  const FilterBand band = filter_band(p.pack_cutsq, *p.coord_bound);
+  const bool exact_rules = p.unique_rule != 0;
+  const float4 *pos4f = reinterpret_cast<const float4 *>(p.pos4);
   for (int g = blockIdx.x; g < groups; g += gridDim.x) {
     const int row0 = g * kWarpsPerBlock;
     if (threadIdx.x < kWarpsPerBlock) {
@@ -286,6 +318,7 @@ __global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
     if (row < p.inum && i < 0 && lane == 0) p.ccount[row] = 0;
     if (row < p.inum && i >= 0) {
       const double4 xi = load4(p.xd4 + i);
+      const float4 fi = __ldg(pos4f + i);
       const int si = static_cast<int>(xi.w);
       int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
       const long long rowbase = static_cast<long long>(i) * p.atom_stride;
@@ -295,36 +328,48 @@ __global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
       // Write out and evaluate the first `count` queued pairs (count <= 32), then drop them.
       auto flush = [&](int count) {
         __syncwarp();
-        int j = 0, sj = 0;
-        T r2 = T(0);
+        int j = 0;
+        float r2f = 0.0f;
         if (lane < count) {
           j = qj[lane];
-          r2 = qr2[lane];
-          sj = qs[lane];
+          r2f = qr2[lane];
         }
-        int tj = 0, ts = 0;
-        T tr2 = T(0);
+        int tj = 0;
+        float tr2 = 0.0f;
         const int rest = q - count;
         if (lane < rest) {
           tj = qj[count + lane];
           tr2 = qr2[count + lane];
-          ts = qs[count + lane];
         }
         __syncwarp();
         if (lane < rest) {
           qj[lane] = tj;
           qr2[lane] = tr2;
-          qs[lane] = static_cast<unsigned char>(ts);
         }
         __syncwarp();
         if (lane < count) {
           const int slot = kept + lane;
           if (slot < p.row_cap) crow[slot] = j;
-          if (MODE != kCompactOnly && r2 < p.model_cutsq) {
-            const T r = sqrt(r2);
-            rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
-            if (MODE == kDensityHalf)
-              atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+          if (MODE != kCompactOnly) {
+            T r2;
+            int sj;
+            if constexpr (sizeof(T) == 8) {
+              // The model's double r^2 is the reference's pack r^2 (same operands and order).
+              const double4 xj = load4(p.xd4 + j);
+              const double dx = __dsub_rn(xi.x, xj.x), dy = __dsub_rn(xi.y, xj.y),
+                           dz = __dsub_rn(xi.z, xj.z);
+              r2 = __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
+              sj = static_cast<int>(xj.w);
+            } else {
+              r2 = r2f;
+              sj = static_cast<int>(__ldg(&pos4f[j].w));
+            }
+            if (r2 < p.model_cutsq) {
+              const T r = sqrt(r2);
+              rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+              if (MODE == kDensityHalf)
+                atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+            }
           }
         }
         kept += count;
@@ -332,20 +377,24 @@ __global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
       };
       for (int base = 0; base < n; base += kWarp) {
         const int jj = base + lane;
-        int j = 0, sj = 0;
+        int j = 0;
         bool keep = false;
-        T r2m = T(0);
+        float r2f = 0.0f;
         if (jj < n) {
           j = jj < kTileSlots ? s_tile[jj][warp]
                               : (p.neighbors[rowbase + static_cast<long long>(jj) * p.slot_stride] &
                                  kNeighMask);
           if (j < p.max_atoms) {
-            const double4 xj = load4(p.xd4 + j);
-            keep = pack_keep(p, i, xi, j, xj);
-            if (keep) {
-              const T dx = T(xj.x) - T(xi.x), dy = T(xj.y) - T(xi.y), dz = T(xj.z) - T(xi.z);
-              r2m = dx * dx + dy * dy + dz * dz;
-              sj = static_cast<int>(xj.w);
+            // Float pre-filter; only pairs inside the rounding band, or rows that need the
+            // unique-boundary coordinate rule, read the double coordinates.
+            const float4 fj = __ldg(pos4f + j);
+            const float dx = fj.x - fi.x, dy = fj.y - fi.y, dz = fj.z - fi.z;
+            r2f = dx * dx + dy * dy + dz * dz;
+            if (r2f <= band.hi) {
+              if (r2f < band.lo && !exact_rules)
+                keep = !(p.half_rule && j < i);
+              else
+                keep = pack_keep(p, i, xi, j, load4(p.xd4 + j));
             }
           }
         }
@@ -353,8 +402,7 @@ __global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
         if (keep) {
           const int at = q + __popc(m & below);
           qj[at] = j;
-          qr2[at] = r2m;
-          qs[at] = static_cast<unsigned char>(sj);
+          qr2[at] = r2f;
         }
         q += __popc(m);
         if (q >= kWarp) flush(kWarp);
@@ -409,49 +457,53 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
 }
 
 // One EAM edge (i -> j) of the force pass; python/lammps_jax/eam.py:383-398 for the pair force
-// and :300-309 for the pair energy. Accumulates the row's force and the thread's energy/virial.
+// and :300-309 for the pair energy. r and 1/r come from one reciprocal square root; the density
+// and pair tables share the r grid, so one (node, t) serves both lookups; F' of the density
+// comes from the pre-scaled slope table. Accumulates the row force and the thread's pair energy
+// and virial (both without their constant weights, applied once per block).
 template <typename T, int MODE>
 __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T>::type &pi,
-                                         int si, T fpi, int j, T &fx, T &fy, T &fz, double &e,
-                                         double (&v)[6])
+                                         int si, T fpi, int j, const typename Vec4<T>::type &pj,
+                                         T fpj, T &fx, T &fy, T &fz, double &e, double (&v)[6])
 {
-  typename Vec4<T>::type pj;
-  if constexpr (sizeof(T) == 8) {
-    pj = load4(p.xd4 + j);
-  } else {
-    pj = load4(p.pos4 + j);
-  }
   const T dx = pj.x - pi.x, dy = pj.y - pi.y, dz = pj.z - pi.z;
   const T r2 = dx * dx + dy * dy + dz * dz;
   if (!(r2 < p.model_cutsq)) return;
-  const T r = sqrt(r2);
-  const T rinv = T(1) / r;
+  const T rinv = rsqrt(r2);
+  const T r = r2 * rinv;
+  const T idx = r * p.inv_dr;
+  const T fl = fmin(floor(idx), T(p.nr - 2));
+  const int node = static_cast<int>(fl);
+  const T t = fmin(idx - fl, T(1));
   const int sj = static_cast<int>(pj.w);
-  const T rhojp = spline_s<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
-  T z2, z2p;
-  spline_vs<T>(p.pair + pair_row(si, sj) * p.nr, p.nr, r, p.inv_dr, z2, z2p);
+  const auto dj = load4(p.density_slope + sj * p.nr + node);
+  const T rhojp = dj.x + t * (dj.y + t * dj.z);
+  const auto c = load4(p.pair + pair_row(si, sj) * p.nr + node);
+  const T z2 = c.x + t * (c.y + t * (c.z + t * c.w));
+  const T z2p = (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * p.inv_dr;
   const T phi = z2 * rinv;
   const T phip = (z2p - phi) * rinv;
   T psip;
   if (MODE == kGhost) {
     psip = fpi * rhojp + T(0.5) * phip;
+  } else if (si == sj) {
+    psip = (fpi + fpj) * rhojp + phip;
   } else {
-    const T rhoip = (si == sj) ? rhojp : spline_s<T>(p.density + si * p.nr, p.nr, r, p.inv_dr);
-    psip = fpi * rhojp + __ldg(p.fp + j) * rhoip + phip;
+    const auto di = load4(p.density_slope + si * p.nr + node);
+    psip = fpi * rhojp + fpj * (di.x + t * (di.y + t * di.z)) + phip;
   }
   const T sc = psip * rinv;
   const T ex = sc * dx, ey = sc * dy, ez = sc * dz;
   fx += ex;
   fy += ey;
   fz += ez;
-  e += static_cast<double>(MODE == kHalf ? phi : T(0.5) * phi);
-  const double w = MODE == kRowsFull ? 0.5 : 1.0;
-  v[0] -= w * static_cast<double>(dx * ex);
-  v[1] -= w * static_cast<double>(dy * ey);
-  v[2] -= w * static_cast<double>(dz * ez);
-  v[3] -= w * static_cast<double>(dx * ey);
-  v[4] -= w * static_cast<double>(dx * ez);
-  v[5] -= w * static_cast<double>(dy * ez);
+  e += static_cast<double>(phi);
+  v[0] += static_cast<double>(dx * ex);
+  v[1] += static_cast<double>(dy * ey);
+  v[2] += static_cast<double>(dz * ez);
+  v[3] += static_cast<double>(dx * ey);
+  v[4] += static_cast<double>(dx * ez);
+  v[5] += static_cast<double>(dy * ez);
   if (MODE != kRowsFull && j < p.nall) {
     atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
     atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
@@ -459,11 +511,23 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   }
 }
 
-// a9..a13: fused force + pair energy + virial over the compacted rows. Spilled rows (more kept
-// pairs than row_cap) re-walk the LAMMPS list with the same filter.
+template <typename T>
+__device__ __forceinline__ typename Vec4<T>::type load_pos(const Step<T> &p, int j)
+{
+  if constexpr (sizeof(T) == 8) {
+    return load4(p.xd4 + j);
+  } else {
+    return load4(p.pos4 + j);
+  }
+}
+
+// a9..a13: fused force + pair energy + virial over the compacted rows. Each lane prefetches its
+// next edge's neighbor record and F' one iteration ahead. Spilled rows (more kept pairs than
+// row_cap) re-walk the LAMMPS list with the same filter.
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
 {
+  using V = typename Vec4<T>::type;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double e = 0.0;
   double v[6] = {0, 0, 0, 0, 0, 0};
@@ -472,18 +536,26 @@ __global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
     const int i = p.ilist[row];
     if (i >= p.max_atoms) continue;
     const int n = p.ccount[row];
-    typename Vec4<T>::type pi;
-    if constexpr (sizeof(T) == 8) {
-      pi = load4(p.xd4 + i);
-    } else {
-      pi = load4(p.pos4 + i);
-    }
+    const V pi = load_pos(p, i);
     const int si = static_cast<int>(pi.w);
     const T fpi = p.fp[i];
     T fx = T(0), fy = T(0), fz = T(0);
     if (n <= p.row_cap) {
       const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
-      for (int k = lane; k < n; k += kWarp) eam_edge<T, MODE>(p, pi, si, fpi, crow[k], fx, fy, fz, e, v);
+      int jn = lane < n ? crow[lane] : 0;
+      V pn = lane < n ? load_pos(p, jn) : pi;
+      T fn = (MODE != kGhost && lane < n) ? __ldg(p.fp + jn) : T(0);
+      for (int k = lane; k < n; k += kWarp) {
+        const int j = jn;
+        const V pj = pn;
+        const T fpj = fn;
+        if (k + kWarp < n) {
+          jn = crow[k + kWarp];
+          pn = load_pos(p, jn);
+          if (MODE != kGhost) fn = __ldg(p.fp + jn);
+        }
+        eam_edge<T, MODE>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v);
+      }
     } else {
       const double4 xi = load4(p.xd4 + i);
       const int listed = min(p.numneigh[i], p.maxneighs);
@@ -492,7 +564,8 @@ __global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
         const int j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
         if (j >= p.max_atoms) continue;
         if (pack_keep(p, i, xi, j, load4(p.xd4 + j)))
-          eam_edge<T, MODE>(p, pi, si, fpi, j, fx, fy, fz, e, v);
+          eam_edge<T, MODE>(p, pi, si, fpi, j, load_pos(p, j),
+                            MODE != kGhost ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
       }
     }
     fx = warp_sum(fx);
@@ -511,7 +584,12 @@ __global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
       }
     }
   }
-  double acc[8] = {e, v[0], v[1], v[2], v[3], v[4], v[5], 0.0};
+  // Pair energy: phi/2 per directed edge of a full list, phi per edge of a half list. Virial:
+  // -1/2 rij (x) F_e when every pair appears in two rows, -rij (x) F_e when the receiver takes
+  // -F_e (newton-on scatters).
+  const double ew = MODE == kHalf ? 1.0 : 0.5;
+  const double vw = MODE == kRowsFull ? -0.5 : -1.0;
+  double acc[8] = {ew * e, vw * v[0], vw * v[1], vw * v[2], vw * v[3], vw * v[4], vw * v[5], 0.0};
   store_partials(acc, 0, p.partials);
 }
 
