@@ -217,6 +217,28 @@ ljx_status ljx_halo_forward_self(void *stream, void *rows, int width, int elem_b
 ljx_status ljx_halo_reverse_self(void *stream, void *rows, int width, int elem_bytes,
                                  const int *owner, int first, int n);
 
+/* ---------------------------------------------------------------------------------------------
+ * Allocation-free LJ force pass. No counterpart in the reference: the reference always runs
+ * through a PJRT client that owns its buffers. This is for callers that cannot call cudaMalloc
+ * — a process where another framework already reserved the device memory (JAX/XLA preallocates
+ * most of the GPU by default) or host code bound to a memory pool it does not own. It runs the
+ * same kernels as ljx_force on an lj/cut bundle without an engine: the caller passes inputs and
+ * outputs (atoms->f is accumulated with +=; `result` is device memory for 9 doubles: energy,
+ * virial[6] (both times `scale`), kept pairs, widest list row) and the scratch is a fixed
+ * LJX_NOALLOC_BYTES device array inside the library, held by every GPU that loads it until the
+ * process exits. nlocal + nghost (and inum) must not exceed LJX_NOALLOC_MAX_ATOMS; larger
+ * systems get LJX_ERR_CAPACITY before anything is launched. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress, once per device): make that first call
+ * before any stream capture. Calls share the one array, so calls that overlap on the GPU (other
+ * streams, other host threads) race; serialize them. Nothing here calls cudaMalloc or cudaFree.
+ * force_layout/newton_pair select the distribution exactly as for an lj/cut bundle.
+ * ------------------------------------------------------------------------------------------- */
+#define LJX_NOALLOC_MAX_ATOMS 32768
+#define LJX_NOALLOC_BYTES (2u << 20)
+ljx_status ljx_lj_force_noalloc(void *stream, const ljx_atoms *atoms, const ljx_list *list,
+                                double epsilon, double sigma, double cutoff, int precision,
+                                int force_layout, int newton_pair, double scale, double *result);
+
 /* Number of this library's kernel launches issued since the engine was created. */
 long long ljx_engine_launches(const ljx_engine *engine);
 

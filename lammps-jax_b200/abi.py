@@ -95,6 +95,9 @@ SIGNATURES = [
     ("ljx_comm_zero_rows", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]),
     ("ljx_halo_forward_self", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_int]),
     ("ljx_halo_reverse_self", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_int]),
+    ("ljx_lj_force_noalloc", c_int, [c_void_p, POINTER(Atoms), POINTER(NeighList), c_double,
+                                     c_double, c_double, c_int, c_int, c_int, c_double,
+                                     c_void_p]),
     ("ljx_engine_launches", c_longlong, [c_void_p]),
     ("ljx_version", c_char_p, []),
     ("ljx_neigh_build", c_int, [c_void_p, c_void_p, c_int, c_int, c_double, c_int, c_void_p,

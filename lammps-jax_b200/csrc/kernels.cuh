@@ -682,7 +682,7 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
 }
 
 // Row counts -> exclusive offsets for the reference edge ABI (single block; off the hot path).
-__global__ void k_scan_counts(const int *counts, int n, int per_pair, long long *offsets)
+static __global__ void k_scan_counts(const int *counts, int n, int per_pair, long long *offsets)
 {
   __shared__ long long s_part[1024];
   const int t = threadIdx.x, nt = blockDim.x;
@@ -764,7 +764,7 @@ k_emit_edges(const Step<T> p, const long long *offsets, int duplicate, int max_e
 
 // Padding past the new count up to the previous count (ResetEdgeTailFunctor,
 // cpp/pair_jax_kokkos.cpp:157-173); both counts are read on the device.
-__global__ void k_reset_tail(const long long *count_now, long long *count_prev, int max_atoms,
+static __global__ void k_reset_tail(const long long *count_now, long long *count_prev, int max_atoms,
                              int max_edges, int *senders, int *receivers, uint8_t *mask)
 {
   const long long now = *count_now;
@@ -778,7 +778,7 @@ __global__ void k_reset_tail(const long long *count_now, long long *count_prev, 
   }
 }
 
-__global__ void k_store_prev(const long long *count_now, long long *count_prev)
+static __global__ void k_store_prev(const long long *count_now, long long *count_prev)
 {
   *count_prev = *count_now;
 }
@@ -790,7 +790,7 @@ struct PartialSet {
   int blocks[4];
 };
 
-__global__ void __launch_bounds__(kBlock) k_finalize(PartialSet set, double scale, double *result)
+static __global__ void __launch_bounds__(kBlock) k_finalize(PartialSet set, double scale, double *result)
 {
   __shared__ double s[9][kBlock];
   const int t = threadIdx.x;
@@ -814,7 +814,7 @@ __global__ void __launch_bounds__(kBlock) k_finalize(PartialSet set, double scal
 
 // ---- comm rows (cpp/pair_jax_kokkos.cpp:247-318) ----
 
-__global__ void k_pack_words_by_list(const uint32_t *rows, int words, const int *sendlist, int n,
+static __global__ void k_pack_words_by_list(const uint32_t *rows, int words, const int *sendlist, int n,
                                      double *buf, int slots)
 {
   const long long total = static_cast<long long>(n) * words;
@@ -827,7 +827,7 @@ __global__ void k_pack_words_by_list(const uint32_t *rows, int words, const int 
   }
 }
 
-__global__ void k_unpack_words_at(uint32_t *rows, int words, int first, int n, const double *buf,
+static __global__ void k_unpack_words_at(uint32_t *rows, int words, int first, int n, const double *buf,
                                   int slots)
 {
   const long long total = static_cast<long long>(n) * words;
@@ -839,7 +839,7 @@ __global__ void k_unpack_words_at(uint32_t *rows, int words, int first, int n, c
   }
 }
 
-__global__ void k_pack_words_at(const uint32_t *rows, int words, int first, int n, double *buf,
+static __global__ void k_pack_words_at(const uint32_t *rows, int words, int first, int n, double *buf,
                                 int slots)
 {
   const long long total = static_cast<long long>(n) * words;
