@@ -21,6 +21,27 @@ constexpr int kPartialWidth = 10;
 // straight from global memory), and the per-warp queue of kept pairs.
 constexpr int kTileSlots = 384;
 constexpr int kQueue = 64;
+// Minimum resident blocks per SM requested from the compiler for the two row kernels (caps
+// their registers per thread); 0 leaves the choice to the compiler.
+#ifndef LJX_DENSITY_MIN_BLOCKS
+#define LJX_DENSITY_MIN_BLOCKS 7
+#endif
+#ifndef LJX_FORCE_MIN_BLOCKS
+#define LJX_FORCE_MIN_BLOCKS 4
+#endif
+#ifndef LJX_FORCE_PREFETCH
+#define LJX_FORCE_PREFETCH 0
+#endif
+#if LJX_DENSITY_MIN_BLOCKS > 0
+#define LJX_DENSITY_BOUNDS __launch_bounds__(kBlock, LJX_DENSITY_MIN_BLOCKS)
+#else
+#define LJX_DENSITY_BOUNDS __launch_bounds__(kBlock)
+#endif
+#if LJX_FORCE_MIN_BLOCKS > 0
+#define LJX_FORCE_BOUNDS __launch_bounds__(kBlock, LJX_FORCE_MIN_BLOCKS)
+#else
+#define LJX_FORCE_BOUNDS __launch_bounds__(kBlock)
+#endif
 
 enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2 };
 // Force distribution modes.
@@ -263,7 +284,7 @@ __device__ __forceinline__ FilterBand filter_band(double cutsq, unsigned int bou
 // segment of the compacted row and evaluated by all 32 lanes together (sqrt + density spline),
 // so the floating-point work runs at full lane occupancy instead of at the ~40% keep rate.
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kBlock) k_density(const Step<T> p)
+__global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
 {
   __shared__ int s_tile[kTileSlots][kWarpsPerBlock + 1];
   __shared__ int s_row_i[kWarpsPerBlock];
@@ -525,7 +546,7 @@ __device__ __forceinline__ typename Vec4<T>::type load_pos(const Step<T> &p, int
 // next edge's neighbor record and F' one iteration ahead. Spilled rows (more kept pairs than
 // row_cap) re-walk the LAMMPS list with the same filter.
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
+__global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
 {
   using V = typename Vec4<T>::type;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -540,7 +561,14 @@ __global__ void __launch_bounds__(kBlock) k_force(const Step<T> p)
     const int si = static_cast<int>(pi.w);
     const T fpi = p.fp[i];
     T fx = T(0), fy = T(0), fz = T(0);
-    if (n <= p.row_cap) {
+    if (n <= p.row_cap && !LJX_FORCE_PREFETCH) {
+      const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
+      for (int k = lane; k < n; k += kWarp) {
+        const int j = crow[k];
+        eam_edge<T, MODE>(p, pi, si, fpi, j, load_pos(p, j),
+                          MODE != kGhost ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
+      }
+    } else if (n <= p.row_cap) {
       const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
       int jn = lane < n ? crow[lane] : 0;
       V pn = lane < n ? load_pos(p, jn) : pi;
