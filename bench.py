@@ -143,7 +143,9 @@ def run_ljx(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=180))
     cells = (args.cells, args.cells, args.cells)
     precision = args.precision
     if world > 1:
@@ -175,6 +177,12 @@ def run_ljx(args):
         eng.force(atoms, nl, False, 1.0)
         mark(5)
         res = eng.read_result()
+        if world > 1:
+            # Collective capacity check, as the pair style's MPI_Allreduce after execution.
+            flags = torch.tensor([res.edge_count, res.overflow], device="cuda")
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+            if int(flags[1].item()):
+                raise RuntimeError("LAMMPS-JAX edge capacity exceeded")
         mark(6)
         return res
 
@@ -292,7 +300,37 @@ def setup_single(ljx, cells, precision):
 
 
 def setup_decomposed(ljx, cells, rank, world, precision, local):
-    raise SystemExit("multi-GPU spatial decomposition is not wired into bench.py yet")
+    """Rank `rank` of a z-slab decomposition: 2,048,000 owned atoms per rank (weak scaling)."""
+    import tempfile
+
+    import torch
+    from importlib import import_module
+    halo = import_module("lammps_jax_b200.halo")
+    slab = ljx.synth.slab_decomposition(cells, A_CU, JITTER, 2024, rank, world, CUTOFF + SKIN)
+    nlocal, nall = slab.nlocal, len(slab.x)
+    text = ljx.synth.synthetic_setfl(("Cu",))
+    tmp = Path(tempfile.mkdtemp())
+    path = tmp / f"c3_rank{rank}.json"
+    max_atoms = nall + 1024
+    ljx.write_bundle(path, potential=ljx.eam_potential(text), max_atoms=max_atoms,
+                     max_edges=max_atoms * 128, cutoff=CUTOFF, unit_style="metal",
+                     precision=precision, force_output="atom-force", newton="off", comm=True,
+                     n_species=1)
+    x = torch.as_tensor(slab.x, device="cuda")
+    system = ljx.System(x=x, type=torch.as_tensor(slab.types, device="cuda"),
+                        f=torch.zeros_like(x), nlocal=nlocal, nghost=nall - nlocal,
+                        newton_pair=False, unit_style="metal", ntypes=1)
+    pair = ljx.PairJax(device=local)
+    pair.coeff(system, "*", "*", str(path))
+    pair.init_style(system)
+    system.list = ljx.synth.neighbor_list(slab.x, nlocal, CUTOFF + SKIN, half=False)
+    elem = 8 if precision == "float64" else 4
+    system.comm = halo.SlabExchange(slab, 1, elem)
+    return system, nlocal, nall, {
+        "pair": pair, "comm_launches": system.comm.launches_per_exchange,
+        "parallelism": f"z-slab spatial decomposition over {world} GPUs, F'(rho) halo by "
+                       "grouped NCCL send/recv with both z-neighbors + x/y periodic images",
+        "close": lambda: None}
 
 
 def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall, world):
