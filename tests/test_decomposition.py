@@ -47,6 +47,16 @@ def test_ghost_rows_are_neighbor_send_lists(ljx, nranks):
         assert np.all(s.x[:s.nlocal, 2] >= s.zlo) and np.all(s.x[:s.nlocal, 2] < s.zhi)
 
 
+def test_slabs_tile_the_crystal_without_overlap(ljx):
+    """Owned atoms of all ranks form one physical crystal: no site duplicated across a face."""
+    from scipy.spatial import cKDTree
+    parts = slabs(ljx, 3)
+    x = np.concatenate([p.x[:p.nlocal] for p in parts])
+    assert len(x) == 3 * 4 * np.prod(CELLS)
+    tree = cKDTree(x, boxsize=parts[0].box)
+    assert not tree.query_pairs(1.5)
+
+
 def combined_owner(parts):
     """Owner (in the combined owned index space) of every ghost row of every rank."""
     nranks = len(parts)
