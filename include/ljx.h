@@ -120,7 +120,15 @@ typedef struct ljx_atoms {
 
 /* A NeighListKokkos view: row ii lists atom ilist[ii]; its jj-th neighbor is
  * neighbors[i * atom_stride + jj * slot_stride] & NEIGHMASK for jj < numneigh[i] (Kokkos
- * LayoutLeft on CUDA: atom_stride 1, slot_stride = list allocation rows). */
+ * LayoutLeft on CUDA: atom_stride 1, slot_stride = list allocation rows).
+ *
+ * ago is LAMMPS's neighbor->ago: steps since this list was built, 0 on the step it was built
+ * (the reference's neighbor-matrix path repacks on the same signal, cpp/pair_jax_kokkos.cpp:
+ * 1011-1012). For EAM, ljx_density caches per group of 8 rows the union of their neighbors
+ * within rc plus a margin when ago == 0, and reuses it while ago > 0. It rebuilds by itself when
+ * the list pointers or sizes change or when some atom has moved more than half the margin. The
+ * kept pairs are the reference's in every case. A negative ago turns the cache off: every step
+ * then filters the whole list, as the reference's sparse-edge path does. */
 typedef struct ljx_list {
   const int *ilist;
   const int *numneigh;
@@ -130,6 +138,7 @@ typedef struct ljx_list {
   int inum;
   int gnum;
   int maxneighs;
+  int ago;
 } ljx_list;
 
 /* Per-step results; energy and virial already multiplied by the pair_coeff scale. */

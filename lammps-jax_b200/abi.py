@@ -47,7 +47,7 @@ class Atoms(Structure):
 class NeighList(Structure):
     _fields_ = [("ilist", c_void_p), ("numneigh", c_void_p), ("neighbors", c_void_p),
                 ("atom_stride", c_longlong), ("slot_stride", c_longlong), ("inum", c_int),
-                ("gnum", c_int), ("maxneighs", c_int)]
+                ("gnum", c_int), ("maxneighs", c_int), ("ago", c_int)]
 
 
 class Result(Structure):

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -15,6 +16,7 @@
 #include <vector>
 
 #include "bundle.h"
+#include "groups.cuh"
 #include "kernels.cuh"
 #include "ljx.h"
 
@@ -75,7 +77,31 @@ struct ljx_engine {
   void *density = nullptr;
   void *density_slope = nullptr;
   void *pair = nullptr;
-  unsigned int *coord_bound = nullptr;
+  unsigned int *coord_bound = nullptr;  // [0] largest |coordinate|, [1] largest displacement^2
+  // Row-group candidate cache (EAM bundles).
+  double4 *xref = nullptr;
+  int *gatom = nullptr;
+  int *gcount = nullptr;
+  unsigned short *rslot = nullptr;
+  int *rcount = nullptr;
+  int gcap = 0;
+  int rcap = 0;
+  int groups_cap = 0;
+  struct GroupKey {
+    const int *ilist, *numneigh, *neighbors;
+    long long atom_stride, slot_stride;
+    int inum, maxneighs, nlocal, nall, half_rule, unique_rule;
+    bool operator==(const GroupKey &o) const
+    {
+      return ilist == o.ilist && numneigh == o.numneigh && neighbors == o.neighbors &&
+             atom_stride == o.atom_stride && slot_stride == o.slot_stride && inum == o.inum &&
+             maxneighs == o.maxneighs && nlocal == o.nlocal && nall == o.nall &&
+             half_rule == o.half_rule && unique_rule == o.unique_rule;
+    }
+  };
+  bool groups_valid = false;
+  GroupKey groups_key{};
+  long long group_builds = 0;  // host-requested cache builds
   int *senders = nullptr;
   int *receivers = nullptr;
   uint8_t *edge_mask = nullptr;
@@ -97,7 +123,8 @@ struct ljx_engine {
   {
     cudaSetDevice(device);
     void *ptrs[] = {xd4,       pos4,      rho,        fp,          cedges,  ccount,
-                    embedding, density,   density_slope, pair,     coord_bound, senders,
+                    embedding, density,   density_slope, pair,     coord_bound, xref,
+                    gatom,     gcount,    rslot,      rcount,      senders,
                     receivers, edge_mask, offsets,    count_prev,  partials, result};
     for (void *p : ptrs)
       if (p) cudaFree(p);
@@ -255,6 +282,14 @@ ljx::Step<T> make_step(ljx_engine *e, const ljx_atoms *a, const ljx_list *l, dou
   p.density_slope = static_cast<const V *>(e->density_slope);
   p.pair = static_cast<const V *>(e->pair);
   p.coord_bound = e->coord_bound;
+  p.disp_bound = e->coord_bound + 1;
+  p.xref = e->xref;
+  p.gatom = e->gatom;
+  p.gcount = e->gcount;
+  p.gcap = e->gcap;
+  p.rslot = e->rslot;
+  p.rcount = e->rcount;
+  p.rcap = e->rcap;
   p.n_species = e->c.potential == LJX_POTENTIAL_EAM ? std::max(1, e->bundle.eam.n_elements) : 1;
   p.nrho = e->bundle.eam.nrho;
   p.nr = e->bundle.eam.nr;
@@ -344,6 +379,57 @@ void launch_density(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
       ljx::k_density<T, ljx::kDensityFull><<<grid, ljx::kBlock, 0, s>>>(p);
   }
   check_launch("k_density");
+  e->launches++;
+  e->step_blocks[kDensityPart] = grid;
+}
+
+// Cache margin as a fraction of the pack cutoff: unions hold pairs within rc (1 + margin) and
+// stay valid until some atom has moved rc * margin / 2.
+constexpr double kGroupMargin = 0.08;
+
+template <typename T>
+void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago, int mode)
+{
+  if (p.inum <= 0) return;
+  const ljx_engine::GroupKey key{p.ilist,      p.numneigh, p.neighbors, p.atom_stride,
+                                 p.slot_stride, p.inum,     p.maxneighs, p.nlocal,
+                                 p.nall,        p.half_rule, p.unique_rule};
+  const bool rebuild = ago == 0 || !e->groups_valid || !(key == e->groups_key);
+  const double rc = std::sqrt(p.pack_cutsq);
+  const double half_margin = 0.5 * kGroupMargin * rc;
+  // Rounded down: the device rebuilds as soon as the float displacement^2 passes it.
+  const float disp_limit = std::nextafter(static_cast<float>(half_margin * half_margin), 0.0f);
+  const double cand = rc * (1.0 + kGroupMargin);
+  const int span = std::min(p.nall, e->c.max_atoms);
+  const int groups = (p.inum + ljx::kGroupRows - 1) / ljx::kGroupRows;
+  static int build_per_sm = 0;
+  if (build_per_sm == 0) {
+    check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&build_per_sm, ljx::k_build_groups<T>,
+                                                        ljx::kBuildBlock, 0),
+          "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    build_per_sm = std::max(1, build_per_sm);
+  }
+  const int bgrid = std::max(1, std::min((groups + ljx::kBuildWarps - 1) / ljx::kBuildWarps,
+                                         e->sm_count * build_per_sm));
+  ljx::k_build_groups<T><<<bgrid, ljx::kBuildBlock, 0, s>>>(p, span, rebuild ? 1 : 0, disp_limit,
+                                                            cand * cand);
+  check_launch("k_build_groups");
+  e->launches++;
+  if (rebuild) e->group_builds++;
+  e->groups_valid = true;
+  e->groups_key = key;
+  int grid = 0;
+  const int need = groups;  // one block per group
+  if (mode == ljx::kDensityHalf) {
+    grid = std::max(1, std::min(need, std::min(e->max_grid, e->sm_count * blocks_per_sm(
+                                                            ljx::k_density_groups<T, ljx::kDensityHalf>))));
+    ljx::k_density_groups<T, ljx::kDensityHalf><<<grid, ljx::kBlock, 0, s>>>(p);
+  } else {
+    grid = std::max(1, std::min(need, std::min(e->max_grid, e->sm_count * blocks_per_sm(
+                                                            ljx::k_density_groups<T, ljx::kDensityFull>))));
+    ljx::k_density_groups<T, ljx::kDensityFull><<<grid, ljx::kBlock, 0, s>>>(p);
+  }
+  check_launch("k_density_groups");
   e->launches++;
   e->step_blocks[kDensityPart] = grid;
 }
@@ -444,7 +530,11 @@ ljx_status density_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const
     const long long rows = std::min<long long>(p.nall, e->c.max_atoms);
     check(cudaMemsetAsync(e->rho, 0, rows * sizeof(T), s), "cudaMemsetAsync(rho)");
   }
-  launch_density<T>(e, s, p, m.density);
+  if (l->ago < 0 || e->xref == nullptr) {
+    launch_density<T>(e, s, p, m.density);
+  } else {
+    launch_groups<T>(e, s, p, l->ago, m.density);
+  }
   e->last_duplicate = m.duplicate ? 2 : 1;
   return LJX_OK;
 }
@@ -490,7 +580,7 @@ ljx_status pack_atoms_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a)
 {
   ljx::Step<T> p = make_step<T>(e, a, nullptr, 1.0);
   const int span = std::min(p.nall, e->c.max_atoms);
-  check(cudaMemsetAsync(e->coord_bound, 0, sizeof(unsigned int), s), "cudaMemsetAsync(bound)");
+  check(cudaMemsetAsync(e->coord_bound, 0, 2 * sizeof(unsigned int), s), "cudaMemsetAsync(bound)");
   if (span <= 0) return LJX_OK;
   ljx::k_pack_atoms<T><<<flat_grid(span), ljx::kBlock, 0, s>>>(p, span);
   check_launch("k_pack_atoms");
@@ -607,8 +697,27 @@ ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **
     // Float copy of the positions: the distance pre-filter (and the float model) reads it.
     e->pos4 = device_alloc(max_atoms * sizeof(float4), "cudaMalloc(pos4)");
     check(cudaMemset(e->pos4, 0, max_atoms * sizeof(float4)), "cudaMemset(pos4)");
-    e->coord_bound = static_cast<unsigned int *>(device_alloc(sizeof(unsigned int), "cudaMalloc(bound)"));
-    check(cudaMemset(e->coord_bound, 0, sizeof(unsigned int)), "cudaMemset(bound)");
+    e->coord_bound = static_cast<unsigned int *>(device_alloc(2 * sizeof(unsigned int), "cudaMalloc(bound)"));
+    check(cudaMemset(e->coord_bound, 0, 2 * sizeof(unsigned int)), "cudaMemset(bound)");
+    if (c.potential == LJX_POTENTIAL_EAM) {
+      // Candidate cache: a group's union holds about 3.5 rows' worth of kept pairs at solid
+      // densities and a row's candidates within rc (1 + margin) about 1.6; 4 x and 2 x row_cap
+      // leave headroom. Groups that do not fit walk their lists.
+      e->groups_cap = (e->rows_cap + ljx::kGroupRows - 1) / ljx::kGroupRows;
+      e->gcap = std::max(64, std::min(ljx::kUnionMax, 4 * e->row_cap));
+      e->rcap = std::max(32, std::min(ljx::kUnionMax, 2 * e->row_cap));
+      e->xref = static_cast<double4 *>(device_alloc(max_atoms * sizeof(double4), "cudaMalloc(xref)"));
+      check(cudaMemset(e->xref, 0, max_atoms * sizeof(double4)), "cudaMemset(xref)");
+      e->gatom = static_cast<int *>(device_alloc(
+          static_cast<size_t>(e->groups_cap) * e->gcap * sizeof(int), "cudaMalloc(group unions)"));
+      e->gcount = static_cast<int *>(device_alloc(e->groups_cap * sizeof(int), "cudaMalloc(group counts)"));
+      check(cudaMemset(e->gcount, 0, e->groups_cap * sizeof(int)), "cudaMemset(group counts)");
+      e->rslot = static_cast<unsigned short *>(device_alloc(
+          static_cast<size_t>(e->groups_cap) * ljx::kGroupRows * e->rcap * sizeof(unsigned short),
+          "cudaMalloc(row candidates)"));
+      e->rcount = static_cast<int *>(device_alloc(
+          static_cast<size_t>(e->groups_cap) * ljx::kGroupRows * sizeof(int), "cudaMalloc(row counts)"));
+    }
     e->rho = device_alloc(max_atoms * real, "cudaMalloc(rho)");
     e->fp = device_alloc(max_atoms * real, "cudaMalloc(fp)");
     check(cudaMemset(e->rho, 0, max_atoms * real), "cudaMemset(rho)");

@@ -1,0 +1,362 @@
+// Row-group density pass over cached neighbor unions (sm_100a).
+//
+// The list pass (k_density) gathers the float position of every listed pair of every row (about
+// 215 per row at the C3 density, each its own L1 sector) and the double position of every kept
+// pair. Consecutive list rows are spatial neighbours (LAMMPS sorts atoms by bin), so their
+// neighbor sets overlap heavily. When LAMMPS has built a new list (neighbor->ago == 0, the
+// signal the reference's neighbor-matrix path also follows, cpp/pair_jax_kokkos.cpp:1011-1012),
+// k_build_groups stores for each group of kGroupRows consecutive rows:
+//   - the union of the rows' neighbors within rc + margin (about 300 atoms for 8 rows at C3);
+//   - for each row, its candidates within rc + margin as 16-bit slots into that union.
+// Every step, k_density_groups runs one block per group. The block stages the union's positions
+// in shared memory (one global gather per union atom, shared by the eight rows). Then, as in the
+// list pass, one warp per row filters its candidates with the reference's exact keep test,
+// compacts the kept pairs and evaluates the density spline. Per row that is about 40 position
+// gathers from global memory instead of about 300, and about 135 candidates instead of 215 list
+// slots.
+//
+// The kept set is the reference's exactly. A pair the reference keeps is in its row's list and
+// lies within rc now. While no atom has moved more than margin / 2 since the build, it lay
+// within rc + margin then, so it is among its row's candidates. k_pack_atoms tracks the largest
+// displacement; k_build_groups rebuilds on the device when it passes the limit.
+#pragma once
+
+#include "kernels.cuh"
+
+namespace ljx {
+
+constexpr int kGroupRows = 8;          // list rows per group: one block, one warp per row
+constexpr int kHashSlots = 1024;       // per-warp open-addressing set of neighbor indices
+constexpr int kBuildWarps = 8;         // build block: one group per warp
+constexpr int kBuildBlock = kBuildWarps * kWarp;
+constexpr int kUnionMax = 512;         // largest union a group may cache (shared-memory stage)
+
+static_assert(kGroupRows == kWarpsPerBlock, "one warp per row of a group");
+static_assert(kGroupRows <= 8, "row masks are one byte");
+static_assert(kUnionMax < kHashSlots, "the set must keep free slots");
+
+#ifndef LJX_GROUP_MIN_BLOCKS
+#define LJX_GROUP_MIN_BLOCKS 6
+#endif
+#if LJX_GROUP_MIN_BLOCKS > 0
+#define LJX_GROUP_BOUNDS __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS)
+#else
+#define LJX_GROUP_BOUNDS __launch_bounds__(kBlock)
+#endif
+
+// Rebuild the group caches when the host asks (new list, first use, changed sizes or pointers)
+// or when some atom has moved more than margin / 2 since the last build (disp_limit is that
+// squared distance, rounded down). Every block reads the same displacement word, so the
+// decision is uniform over the grid. Also records the positions the displacement is measured
+// from. cand_cutsq is (rc + margin)^2; the float test uses its rounding band, so a pair whose
+// exact distance is within rc + margin is never dropped.
+template <typename T>
+__global__ void __launch_bounds__(kBuildBlock)
+k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, double cand_cutsq)
+{
+  __shared__ int s_key[kBuildWarps][kHashSlots];
+  __shared__ unsigned s_mask[kBuildWarps][kHashSlots / 4];
+  __shared__ unsigned short s_used[kBuildWarps][kUnionMax];
+  if (!force_build && !(__uint_as_float(*p.disp_bound) > disp_limit)) return;
+  for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < span; a += gridDim.x * blockDim.x)
+    p.xref[a] = p.xd4[a];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  int *key = s_key[warp];
+  unsigned *mask = s_mask[warp];
+  unsigned short *used = s_used[warp];
+  const float4 *pos4f = reinterpret_cast<const float4 *>(p.pos4);
+  const FilterBand band = filter_band(cand_cutsq, *p.coord_bound);
+  const int groups = (p.inum + kGroupRows - 1) / kGroupRows;
+  // The set starts empty once; each group then empties only the slots it used.
+  for (int h = lane; h < kHashSlots; h += kWarp) key[h] = -1;
+  for (int h = lane; h < kHashSlots / 4; h += kWarp) mask[h] = 0u;
+  __syncwarp();
+  for (int g = blockIdx.x * kBuildWarps + warp; g < groups; g += gridDim.x * kBuildWarps) {
+    // Lane l walks row l % 8, four slots per step: with LayoutLeft and consecutive rows, one
+    // step reads slot s of all eight rows as one 32-byte sector.
+    const int k = lane & (kGroupRows - 1);
+    const int row = g * kGroupRows + k;
+    int i = -1, n = 0;
+    float4 fi = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < p.inum) {
+      i = p.ilist[row];
+      if (i < p.max_atoms) {
+        n = min(p.numneigh[i], p.maxneighs);
+        fi = __ldg(pos4f + i);
+      } else {
+        i = -1;
+      }
+    }
+    int longest = n;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) longest = max(longest, __shfl_xor_sync(kFull, longest, o));
+    bool lost = false;
+    int total = 0;  // distinct atoms so far (uniform over the warp)
+    const long long rowbase = static_cast<long long>(i) * p.atom_stride;
+    const unsigned bit = 1u << static_cast<unsigned>(k);
+    for (int s0 = 0; s0 < longest; s0 += kWarp / kGroupRows) {
+      const int s = s0 + lane / kGroupRows;
+      bool cand = false;
+      int j = 0;
+      if (i >= 0 && s < n) {
+        j = p.neighbors[rowbase + static_cast<long long>(s) * p.slot_stride] & kNeighMask;
+        if (j < p.max_atoms && !(p.half_rule && j < i)) {
+          const float4 fj = __ldg(pos4f + j);
+          const float dx = fj.x - fi.x, dy = fj.y - fi.y, dz = fj.z - fi.z;
+          cand = dx * dx + dy * dy + dz * dz <= band.hi;
+        }
+      }
+      // Insert j (multiplicative hash, linear probing). The lane that places a new atom
+      // records its slot; the union keeps that first-seen order, which is the order of the
+      // LAMMPS rows' own lists.
+      unsigned h = (static_cast<unsigned>(j) * 0x9E3779B1u) >> 22;
+      bool fresh = false;
+      if (cand) {
+        bool placed = false;
+        for (int probe = 0; probe < kHashSlots; ++probe) {
+          const int cur = atomicCAS(key + h, -1, j);
+          if (cur == -1 || cur == j) {
+            atomicOr(mask + (h >> 2), bit << ((h & 3u) * 8u));
+            fresh = cur == -1;
+            placed = true;
+            break;
+          }
+          h = (h + 1u) & (kHashSlots - 1);
+        }
+        lost |= !placed;
+      }
+      const unsigned m = __ballot_sync(kFull, fresh);
+      if (fresh) {
+        const int at = total + __popc(m & below);
+        if (at < kUnionMax) used[at] = static_cast<unsigned short>(h);
+      }
+      total += __popc(m);
+    }
+    lost = __any_sync(kFull, lost) || total > kUnionMax;
+    __syncwarp();
+    // Union in first-seen order, then each row's candidates as slots into it (union order).
+    const int stored = min(total, kUnionMax);
+    bool spilled = lost || total > p.gcap;
+    if (!spilled) {
+      int *out = p.gatom + static_cast<long long>(g) * p.gcap;
+      for (int at = lane; at < stored; at += kWarp) out[at] = key[used[at]];
+      for (int r = 0; r < kGroupRows && !spilled; ++r) {
+        const int rrow = g * kGroupRows + r;
+        if (rrow >= p.inum) break;
+        unsigned short *slots = p.rslot + static_cast<long long>(rrow) * p.rcap;
+        int got = 0;
+        for (int base = 0; base < stored; base += kWarp) {
+          const int at = base + lane;
+          bool has = false;
+          if (at < stored) {
+            const int h = used[at];
+            has = (mask[h >> 2] >> ((h & 3) * 8 + r)) & 1u;
+          }
+          const unsigned m = __ballot_sync(kFull, has);
+          if (has) {
+            const int pos = got + __popc(m & below);
+            if (pos < p.rcap) slots[pos] = static_cast<unsigned short>(at);
+          }
+          got += __popc(m);
+        }
+        if (lane == 0) p.rcount[rrow] = got;
+        spilled = got > p.rcap;
+      }
+    }
+    __syncwarp();
+    // Empty the used slots for the next group (the whole set if not every slot was recorded).
+    if (total > kUnionMax) {
+      for (int h = lane; h < kHashSlots; h += kWarp) key[h] = -1;
+      for (int h = lane; h < kHashSlots / 4; h += kWarp) mask[h] = 0u;
+    } else {
+      for (int at = lane; at < stored; at += kWarp) {
+        const int h = used[at];
+        key[h] = -1;
+        mask[h >> 2] = 0u;
+      }
+    }
+    __syncwarp();
+    // A group that does not fit is marked past capacity; the density pass then walks its rows'
+    // lists instead.
+    if (lane == 0) p.gcount[g] = spilled ? p.gcap + 1 : total;
+    __syncwarp();
+  }
+}
+
+// a2 + a6 over the group caches: one block per group, one warp per row. The union's positions
+// are staged in shared memory; each warp filters its row's candidates with the reference's exact
+// keep test, compacts the kept pairs into the row's segment of the compacted buffer (the force
+// pass reads it as from k_density) and accumulates the EAM density, scattered to the neighbor as
+// well for half lists. Groups past capacity walk their rows' lists.
+template <typename T, int MODE>
+__global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
+{
+  __shared__ double4 s_x[kUnionMax];
+  __shared__ int s_j[kUnionMax];
+  __shared__ int s_qs[kWarpsPerBlock][kQueue];
+  __shared__ double s_qr2[kWarpsPerBlock][kQueue];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  int *qs = s_qs[warp];
+  double *qr2 = s_qr2[warp];
+  const int groups = (p.inum + kGroupRows - 1) / kGroupRows;
+  double kept_sum = 0.0;
+  int widest = 0;
+  for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+    const int count = p.gcount[g];
+    const bool cached = count <= p.gcap;
+    if (cached) {
+      const int *atoms = p.gatom + static_cast<long long>(g) * p.gcap;
+      for (int t = threadIdx.x; t < count; t += kBlock) {
+        const int j = atoms[t];
+        s_x[t] = load4(p.xd4 + j);
+        s_j[t] = j;
+      }
+    }
+    __syncthreads();
+    const int row = g * kGroupRows + warp;
+    int i = -1;
+    if (row < p.inum) {
+      i = p.ilist[row];
+      if (i >= p.max_atoms) i = -1;
+      if (i < 0 && lane == 0) p.ccount[row] = 0;
+    }
+    if (i >= 0) {
+      const int listed = p.numneigh[i];
+      widest = max(widest, listed);
+      const double4 xi = load4(p.xd4 + i);
+      const float fix = static_cast<float>(xi.x), fiy = static_cast<float>(xi.y),
+                  fiz = static_cast<float>(xi.z);
+      const int si = static_cast<int>(xi.w);
+      int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
+      T rho = T(0);
+      int kept = 0;
+      if (cached) {
+        int q = 0;
+        // Write out and evaluate the first n queued candidates (n <= 32), then drop them.
+        auto flush = [&](int n) {
+          __syncwarp();
+          int slot = 0;
+          double r2d = 0.0;
+          if (lane < n) {
+            slot = qs[lane];
+            r2d = qr2[lane];
+          }
+          const int rest = q - n;
+          int ts = 0;
+          double tr = 0.0;
+          if (lane < rest) {
+            ts = qs[n + lane];
+            tr = qr2[n + lane];
+          }
+          __syncwarp();
+          if (lane < rest) {
+            qs[lane] = ts;
+            qr2[lane] = tr;
+          }
+          __syncwarp();
+          if (lane < n) {
+            const int j = s_j[slot];
+            const int at = kept + lane;
+            if (at < p.row_cap) crow[at] = j;
+            T r2;
+            const double4 xj = s_x[slot];
+            const int sj = static_cast<int>(xj.w);
+            if constexpr (sizeof(T) == 8) {
+              r2 = r2d;  // the model's double r^2 is the reference's pack r^2
+            } else {
+              const float dx = static_cast<float>(xj.x) - fix, dy = static_cast<float>(xj.y) - fiy,
+                          dz = static_cast<float>(xj.z) - fiz;
+              r2 = dx * dx + dy * dy + dz * dz;
+            }
+            if (r2 < p.model_cutsq) {
+              const T r = sqrt(r2);
+              rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+              if (MODE == kDensityHalf)
+                atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+            }
+          }
+          kept += n;
+          q = rest;
+        };
+        const int n = p.rcount[row];
+        const unsigned short *slots = p.rslot + static_cast<long long>(row) * p.rcap;
+        for (int base = 0; base < n; base += kWarp) {
+          int slot = 0;
+          bool keep = false;
+          double r2d = 0.0;
+          if (base + lane < n) {
+            // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
+            // staged coordinates.
+            slot = slots[base + lane];
+            const double4 xj = s_x[slot];
+            r2d = pack_r2(xi, xj);
+            keep = r2d <= p.pack_cutsq && pair_rules(p, i, xi, s_j[slot], xj);
+          }
+          const unsigned m = __ballot_sync(kFull, keep);
+          if (keep) {
+            const int at = q + __popc(m & below);
+            qs[at] = slot;
+            qr2[at] = r2d;
+          }
+          q += __popc(m);
+          if (q >= kWarp) flush(kWarp);
+        }
+        if (q > 0) flush(q);
+      } else {
+        // Group past capacity: walk the row's list with the exact test.
+        const int n = min(listed, p.maxneighs);
+        const long long rowbase = static_cast<long long>(i) * p.atom_stride;
+        for (int base = 0; base < n; base += kWarp) {
+          const int jj = base + lane;
+          bool keep = false;
+          int j = 0;
+          double4 xj = make_double4(0.0, 0.0, 0.0, 0.0);
+          if (jj < n) {
+            j = p.neighbors[rowbase + static_cast<long long>(jj) * p.slot_stride] & kNeighMask;
+            if (j < p.max_atoms) {
+              xj = load4(p.xd4 + j);
+              keep = pack_keep(p, i, xi, j, xj);
+            }
+          }
+          const unsigned m = __ballot_sync(kFull, keep);
+          if (keep) {
+            const int at = kept + __popc(m & below);
+            if (at < p.row_cap) crow[at] = j;
+            T r2;
+            if constexpr (sizeof(T) == 8) {
+              r2 = pack_r2(xi, xj);
+            } else {
+              const float dx = static_cast<float>(xj.x) - fix, dy = static_cast<float>(xj.y) - fiy,
+                          dz = static_cast<float>(xj.z) - fiz;
+              r2 = dx * dx + dy * dy + dz * dz;
+            }
+            if (r2 < p.model_cutsq) {
+              const T r = sqrt(r2);
+              rho += spline_v<T>(p.density + static_cast<int>(xj.w) * p.nr, p.nr, r, p.inv_dr);
+              if (MODE == kDensityHalf)
+                atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+            }
+          }
+          kept += __popc(m);
+        }
+      }
+      rho = warp_sum(rho);
+      if (lane == 0) {
+        if (MODE == kDensityHalf)
+          atomicAdd(p.rho + i, rho);
+        else
+          p.rho[i] = rho;
+        p.ccount[row] = kept;
+      }
+      kept_sum += kept;
+    }
+    __syncthreads();
+  }
+  // kept_sum is carried by every lane of a warp: count it once.
+  double acc[8] = {0, 0, 0, 0, 0, 0, 0, lane == 0 ? kept_sum : 0.0};
+  store_partials(acc, widest, p.partials);
+}
+
+}  // namespace ljx

@@ -117,6 +117,18 @@ struct Step {
   T lj_energy_scale;
   // Largest |coordinate| of this step's atoms (float bits), for the float pre-filter bound.
   unsigned int *coord_bound;
+  // Row-group candidate cache (groups.cuh): positions when the cache was built, the largest
+  // squared displacement since (float bits, rounded up; zeroed with coord_bound), per group of
+  // kGroupRows list rows the union of their neighbors (gatom, gcount), and per row its
+  // candidates as slots into its group's union (rslot, rcount).
+  double4 *xref;
+  unsigned int *disp_bound;
+  int *gatom;
+  int *gcount;
+  int gcap;
+  unsigned short *rslot;
+  int *rcount;
+  int rcap;
   // Per-block partial sums.
   double *partials;
 };
@@ -205,18 +217,23 @@ __device__ __forceinline__ int pair_row(int a, int b)
   return hi * (hi + 1) / 2 + lo;
 }
 
-// The reference's distance filter and pairing rules for list slot (i -> j),
-// cpp/pair_jax_kokkos.cpp:84-101. r^2 is formed without fused multiply-adds so it is the same
-// double the reference computes.
-template <typename T>
-__device__ __forceinline__ bool pack_keep(const Step<T> &p, int i, const double4 &xi, int j,
-                                          const double4 &xj)
+// r^2 of the reference's distance filter, formed without fused multiply-adds so it is the same
+// double the reference computes (cpp/pair_jax_kokkos.cpp:88-91).
+__device__ __forceinline__ double pack_r2(const double4 &xi, const double4 &xj)
 {
   const double dx = __dsub_rn(xi.x, xj.x);
   const double dy = __dsub_rn(xi.y, xj.y);
   const double dz = __dsub_rn(xi.z, xj.z);
-  const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
-  if (r2 > p.pack_cutsq) return false;
+  return __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
+}
+
+// The reference's pairing rules for a pair within the cutoff (cpp/pair_jax_kokkos.cpp:92-101):
+// the j < i half rule, and the unique-boundary rule that keeps a ghost j only if it sorts after
+// i in (z, y, x).
+template <typename T>
+__device__ __forceinline__ bool pair_rules(const Step<T> &p, int i, const double4 &xi, int j,
+                                           const double4 &xj)
+{
   if (p.half_rule && j < i) return false;
   if (p.unique_rule && j >= p.nlocal) {
     if (xj.z < xi.z) return false;
@@ -228,14 +245,28 @@ __device__ __forceinline__ bool pack_keep(const Step<T> &p, int i, const double4
   return true;
 }
 
+// The reference's keep decision for list slot (i -> j), cpp/pair_jax_kokkos.cpp:84-101.
+template <typename T>
+__device__ __forceinline__ bool pack_keep(const Step<T> &p, int i, const double4 &xi, int j,
+                                          const double4 &xj)
+{
+  return pack_r2(xi, xj) <= p.pack_cutsq && pair_rules(p, i, xi, j, xj);
+}
+
 // a1: LAMMPS x/type -> xd4 and its float copy (cpp/pair_jax_kokkos.cpp:35-52), plus the
 // largest |coordinate| (atomic max on float bits; *coord_bound is zeroed before the launch).
 template <typename T>
 __global__ void __launch_bounds__(kBlock) k_pack_atoms(const Step<T> p, int span)
 {
   float big = 0.0f;
+  double moved = 0.0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < span; i += gridDim.x * blockDim.x) {
     const double x0 = p.x[3 * i], x1 = p.x[3 * i + 1], x2 = p.x[3 * i + 2];
+    if (p.xref != nullptr) {
+      const double4 r = p.xref[i];
+      const double d0 = x0 - r.x, d1 = x1 - r.y, d2 = x2 - r.z;
+      moved = fmax(moved, d0 * d0 + d1 * d1 + d2 * d2);
+    }
     // Types past the table map to the last species (the clamped gather of the reference model).
     const int s = min(max(p.type[i] - 1, 0), p.n_species - 1);
     p.xd4[i] = make_double4(x0, x1, x2, static_cast<double>(s));
@@ -247,6 +278,14 @@ __global__ void __launch_bounds__(kBlock) k_pack_atoms(const Step<T> p, int span
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) big = fmaxf(big, __shfl_xor_sync(kFull, big, o));
   if ((threadIdx.x & 31) == 0) atomicMax(p.coord_bound, __float_as_uint(big));
+  if (p.xref != nullptr) {
+    // Rounded up, so the float never understates the displacement (non-negative floats order
+    // like their bit patterns).
+    float m = __double2float_ru(moved);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(p.disp_bound, __float_as_uint(m));
+  }
 }
 
 // Band around rc^2 inside which a float r^2 cannot decide the reference's double test
@@ -271,6 +310,18 @@ __device__ __forceinline__ FilterBand filter_band(double cutsq, unsigned int bou
   b.lo = static_cast<float>(cutsq - d);
   b.hi = static_cast<float>(cutsq + d);
   return b;
+}
+
+// The reference's keep decision for list pair (i -> j) given its float r^2 (from the float copy
+// of the positions) and the band around rc^2: the float value decides outside the band, the
+// double test inside it and wherever the unique-boundary rule needs coordinates.
+template <typename T>
+__device__ __forceinline__ bool keep_pair(const Step<T> &p, const FilterBand &band, float r2f,
+                                          int i, const double4 &xi, int j, const double4 &xj)
+{
+  if (r2f > band.hi) return false;
+  if (r2f < band.lo && !p.unique_rule) return !(p.half_rule && j < i);
+  return pack_keep(p, i, xi, j, xj);
 }
 
 // a2 + a6: filter and compact each list row, accumulating the EAM density.
@@ -377,9 +428,7 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
             if constexpr (sizeof(T) == 8) {
               // The model's double r^2 is the reference's pack r^2 (same operands and order).
               const double4 xj = load4(p.xd4 + j);
-              const double dx = __dsub_rn(xi.x, xj.x), dy = __dsub_rn(xi.y, xj.y),
-                           dz = __dsub_rn(xi.z, xj.z);
-              r2 = __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
+              r2 = pack_r2(xi, xj);
               sj = static_cast<int>(xj.w);
             } else {
               r2 = r2f;

@@ -46,11 +46,14 @@ class NeighborList:
     atom_stride: int = 1
     gnum: int = 0
     half: bool = False
+    # neighbor->ago: steps since the list was built (0 on a build step); negative turns the
+    # engine's per-group candidate cache off.
+    ago: int = 0
 
     def struct(self) -> abi.NeighList:
         return abi.NeighList(self.ilist.data_ptr(), self.numneigh.data_ptr(),
                              self.neighbors.data_ptr(), self.atom_stride, self.slot_stride,
-                             self.inum, self.gnum, self.maxneighs)
+                             self.inum, self.gnum, self.maxneighs, self.ago)
 
 
 @dataclass
