@@ -184,6 +184,12 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
   }
 }
 
+__device__ __forceinline__ double4 staged(const double2 *xy, const double2 *zw, int slot)
+{
+  const double2 a = xy[slot], b = zw[slot];
+  return make_double4(a.x, a.y, b.x, b.y);
+}
+
 // a2 + a6 over the group caches: one block per group, one warp per row. The union's positions
 // are staged in shared memory; each warp filters its row's candidates with the reference's exact
 // keep test, compacts the kept pairs into the row's segment of the compacted buffer (the force
@@ -192,7 +198,10 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
 template <typename T, int MODE>
 __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
 {
-  __shared__ double4 s_x[kUnionMax];
+  // Staged positions as two 16-byte halves: consecutive slots then fall on different bank
+  // quads (a 32-byte record per slot would reach only 4 of the 8 and conflict at least 2-way).
+  __shared__ double2 s_xy[kUnionMax];
+  __shared__ double2 s_zw[kUnionMax];
   __shared__ int s_j[kUnionMax];
   __shared__ int s_qs[kWarpsPerBlock][kQueue];
   __shared__ double s_qr2[kWarpsPerBlock][kQueue];
@@ -210,7 +219,9 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
       const int *atoms = p.gatom + static_cast<long long>(g) * p.gcap;
       for (int t = threadIdx.x; t < count; t += kBlock) {
         const int j = atoms[t];
-        s_x[t] = load4(p.xd4 + j);
+        const double4 xj = load4(p.xd4 + j);
+        s_xy[t] = make_double2(xj.x, xj.y);
+        s_zw[t] = make_double2(xj.z, xj.w);
         s_j[t] = j;
       }
     }
@@ -261,7 +272,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
             const int at = kept + lane;
             if (at < p.row_cap) crow[at] = j;
             T r2;
-            const double4 xj = s_x[slot];
+            const double4 xj = staged(s_xy, s_zw, slot);
             const int sj = static_cast<int>(xj.w);
             if constexpr (sizeof(T) == 8) {
               r2 = r2d;  // the model's double r^2 is the reference's pack r^2
@@ -290,7 +301,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
             // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
             // staged coordinates.
             slot = slots[base + lane];
-            const double4 xj = s_x[slot];
+            const double4 xj = staged(s_xy, s_zw, slot);
             r2d = pack_r2(xi, xj);
             keep = r2d <= p.pack_cutsq && pair_rules(p, i, xi, s_j[slot], xj);
           }
