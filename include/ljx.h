@@ -196,6 +196,14 @@ ljx_status ljx_embed(ljx_engine *engine, void *stream, const ljx_atoms *atoms);
 ljx_status ljx_force(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
                      const ljx_list *list, int newton_pair, double scale);
 
+/* Energy-only evaluation: the reference's execute_energy path for LAMMPS eflag_only steps (MC
+ * moves; cpp/pair_jax_kokkos.cpp:997-1001, 1051-1053, runtime execute_energy). After ljx_density
+ * and ljx_embed (and the reverse rho exchange of half-list plans) it sums the pair energy (EAM)
+ * or the LJ energy; ljx_read_result then reports the total energy. No F' is needed and no force
+ * or virial is written. */
+ljx_status ljx_energy(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
+                      const ljx_list *list, int newton_pair, double scale);
+
 /* Reduces the step's energy/virial/counters and copies them to the host (one stream sync). */
 ljx_status ljx_read_result(ljx_engine *engine, void *stream, ljx_result *out);
 

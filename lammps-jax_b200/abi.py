@@ -82,6 +82,8 @@ SIGNATURES = [
     ("ljx_embed", c_int, [c_void_p, c_void_p, POINTER(Atoms)]),
     ("ljx_force", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
                           c_double]),
+    ("ljx_energy", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
+                           c_double]),
     ("ljx_read_result", c_int, [c_void_p, c_void_p, POINTER(Result)]),
     ("ljx_feature_rows", c_int, [c_void_p, c_int, POINTER(c_void_p), POINTER(c_int),
                                  POINTER(c_int)]),

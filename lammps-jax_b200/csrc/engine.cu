@@ -434,50 +434,50 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   e->step_blocks[kDensityPart] = grid;
 }
 
-template <typename T>
+template <typename T, bool FORCES = true>
 void launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
 {
   if (p.inum <= 0) return;
   int grid = 0;
   switch (mode) {
     case ljx::kGhost:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kGhost>));
-      ljx::k_force<T, ljx::kGhost><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kGhost, FORCES>));
+      ljx::k_force<T, ljx::kGhost, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     case ljx::kHalf:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kHalf>));
-      ljx::k_force<T, ljx::kHalf><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kHalf, FORCES>));
+      ljx::k_force<T, ljx::kHalf, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     default:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kRowsFull>));
-      ljx::k_force<T, ljx::kRowsFull><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kRowsFull, FORCES>));
+      ljx::k_force<T, ljx::kRowsFull, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
   }
   check_launch("k_force");
   e->launches++;
   e->step_blocks[kForcePart] = grid;
 }
 
-template <typename T>
+template <typename T, bool FORCES = true>
 void launch_lj(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
 {
   if (p.inum <= 0) return;
   int grid = 0;
   switch (mode) {
     case ljx::kLjEdgeHalf:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeHalf>));
-      ljx::k_lj<T, ljx::kLjEdgeHalf><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeHalf, FORCES>));
+      ljx::k_lj<T, ljx::kLjEdgeHalf, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     case ljx::kLjAtomFull:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomFull>));
-      ljx::k_lj<T, ljx::kLjAtomFull><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomFull, FORCES>));
+      ljx::k_lj<T, ljx::kLjAtomFull, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     case ljx::kLjAtomHalfPairSum:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomHalfPairSum>));
-      ljx::k_lj<T, ljx::kLjAtomHalfPairSum><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomHalfPairSum, FORCES>));
+      ljx::k_lj<T, ljx::kLjAtomHalfPairSum, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     default:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeFull>));
-      ljx::k_lj<T, ljx::kLjEdgeFull><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeFull, FORCES>));
+      ljx::k_lj<T, ljx::kLjEdgeFull, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
   }
   check_launch("k_lj");
   e->launches++;
@@ -572,6 +572,29 @@ ljx_status force_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const l
   }
   p.partials = e->partial(kForcePart);
   launch_force<T>(e, s, p, m.force);
+  return LJX_OK;
+}
+
+// Energy-only evaluation (the reference's execute_energy path for eflag_only steps,
+// cpp/pair_jax_kokkos.cpp:997-1001,1051-1053): the pair energy over the compacted rows (EAM,
+// after ljx_density and ljx_embed) or the LJ energy over the list. No F' is read and no force or
+// virial is written.
+template <typename T>
+ljx_status energy_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
+                       int newton_pair, double scale)
+{
+  const Modes m = decide_modes(e->c, newton_pair);
+  ljx::Step<T> p = make_step<T>(e, a, l, scale);
+  set_pack_rules(p, e->c, m);
+  e->last_scale = scale;
+  if (e->c.potential == LJX_POTENTIAL_LJ) {
+    p.partials = e->partial(kLjPart);
+    launch_lj<T, false>(e, s, p, m.lj);
+    e->last_duplicate = m.duplicate ? 2 : 1;
+    return LJX_OK;
+  }
+  p.partials = e->partial(kForcePart);
+  launch_force<T, false>(e, s, p, m.force);
   return LJX_OK;
 }
 
@@ -872,6 +895,19 @@ ljx_status ljx_embed(ljx_engine *e, void *stream, const ljx_atoms *atoms)
   return guarded(e, [&]() -> ljx_status {
     auto s = static_cast<cudaStream_t>(stream);
     return e->f64 ? embed_impl<double>(e, s, atoms) : embed_impl<float>(e, s, atoms);
+  });
+}
+
+ljx_status ljx_energy(ljx_engine *e, void *stream, const ljx_atoms *atoms, const ljx_list *list,
+                      int newton_pair, double scale)
+{
+  return guarded(e, [&]() -> ljx_status {
+    const ljx_status st = check_list(e, list);
+    if (st != LJX_OK) return st;
+    if (atoms == nullptr) return fail(e, LJX_ERR_INVALID, "atom arrays are missing");
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? energy_impl<double>(e, s, atoms, list, newton_pair, scale)
+                  : energy_impl<float>(e, s, atoms, list, newton_pair, scale);
   });
 }
 

@@ -29,9 +29,6 @@ constexpr int kQueue = 64;
 #ifndef LJX_FORCE_MIN_BLOCKS
 #define LJX_FORCE_MIN_BLOCKS 4
 #endif
-#ifndef LJX_FORCE_PREFETCH
-#define LJX_FORCE_PREFETCH 0
-#endif
 #if LJX_DENSITY_MIN_BLOCKS > 0
 #define LJX_DENSITY_BOUNDS __launch_bounds__(kBlock, LJX_DENSITY_MIN_BLOCKS)
 #else
@@ -530,8 +527,9 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
 // and :300-309 for the pair energy. r and 1/r come from one reciprocal square root; the density
 // and pair tables share the r grid, so one (node, t) serves both lookups; F' of the density
 // comes from the pre-scaled slope table. Accumulates the row force and the thread's pair energy
-// and virial (both without their constant weights, applied once per block).
-template <typename T, int MODE>
+// and virial (both without their constant weights, applied once per block). Without FORCES only
+// the pair energy is accumulated (energy-only evaluation).
+template <typename T, int MODE, bool FORCES = true>
 __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T>::type &pi,
                                          int si, T fpi, int j, const typename Vec4<T>::type &pj,
                                          T fpj, T &fx, T &fy, T &fz, double &e, double (&v)[6])
@@ -546,38 +544,40 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   const int node = static_cast<int>(fl);
   const T t = fmin(idx - fl, T(1));
   const int sj = static_cast<int>(pj.w);
-  const auto dj = load4(p.density_slope + sj * p.nr + node);
-  const T rhojp = dj.x + t * (dj.y + t * dj.z);
   const auto c = load4(p.pair + pair_row(si, sj) * p.nr + node);
   const T z2 = c.x + t * (c.y + t * (c.z + t * c.w));
-  const T z2p = (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * p.inv_dr;
   const T phi = z2 * rinv;
-  const T phip = (z2p - phi) * rinv;
-  T psip;
-  if (MODE == kGhost) {
-    psip = fpi * rhojp + T(0.5) * phip;
-  } else if (si == sj) {
-    psip = (fpi + fpj) * rhojp + phip;
-  } else {
-    const auto di = load4(p.density_slope + si * p.nr + node);
-    psip = fpi * rhojp + fpj * (di.x + t * (di.y + t * di.z)) + phip;
-  }
-  const T sc = psip * rinv;
-  const T ex = sc * dx, ey = sc * dy, ez = sc * dz;
-  fx += ex;
-  fy += ey;
-  fz += ez;
   e += static_cast<double>(phi);
-  v[0] += static_cast<double>(dx * ex);
-  v[1] += static_cast<double>(dy * ey);
-  v[2] += static_cast<double>(dz * ez);
-  v[3] += static_cast<double>(dx * ey);
-  v[4] += static_cast<double>(dx * ez);
-  v[5] += static_cast<double>(dy * ez);
-  if (MODE != kRowsFull && j < p.nall) {
-    atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
-    atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
-    atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
+  if constexpr (FORCES) {
+    const auto dj = load4(p.density_slope + sj * p.nr + node);
+    const T rhojp = dj.x + t * (dj.y + t * dj.z);
+    const T z2p = (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * p.inv_dr;
+    const T phip = (z2p - phi) * rinv;
+    T psip;
+    if (MODE == kGhost) {
+      psip = fpi * rhojp + T(0.5) * phip;
+    } else if (si == sj) {
+      psip = (fpi + fpj) * rhojp + phip;
+    } else {
+      const auto di = load4(p.density_slope + si * p.nr + node);
+      psip = fpi * rhojp + fpj * (di.x + t * (di.y + t * di.z)) + phip;
+    }
+    const T sc = psip * rinv;
+    const T ex = sc * dx, ey = sc * dy, ez = sc * dz;
+    fx += ex;
+    fy += ey;
+    fz += ez;
+    v[0] += static_cast<double>(dx * ex);
+    v[1] += static_cast<double>(dy * ey);
+    v[2] += static_cast<double>(dz * ez);
+    v[3] += static_cast<double>(dx * ey);
+    v[4] += static_cast<double>(dx * ez);
+    v[5] += static_cast<double>(dy * ez);
+    if (MODE != kRowsFull && j < p.nall) {
+      atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
+      atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
+      atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
+    }
   }
 }
 
@@ -591,16 +591,17 @@ __device__ __forceinline__ typename Vec4<T>::type load_pos(const Step<T> &p, int
   }
 }
 
-// a9..a13: fused force + pair energy + virial over the compacted rows. Each lane prefetches its
-// next edge's neighbor record and F' one iteration ahead. Spilled rows (more kept pairs than
-// row_cap) re-walk the LAMMPS list with the same filter.
-template <typename T, int MODE>
+// a9..a13: fused force + pair energy + virial over the compacted rows. Spilled rows (more kept
+// pairs than row_cap) re-walk the LAMMPS list with the same filter. Without FORCES: the pair
+// energy alone (energy-only evaluation; no F', no force or virial).
+template <typename T, int MODE, bool FORCES = true>
 __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
 {
   using V = typename Vec4<T>::type;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double e = 0.0;
   double v[6] = {0, 0, 0, 0, 0, 0};
+  constexpr bool kNeedFpj = FORCES && MODE != kGhost;
   for (int row = blockIdx.x * kWarpsPerBlock + warp; row < p.inum;
        row += gridDim.x * kWarpsPerBlock) {
     const int i = p.ilist[row];
@@ -608,30 +609,14 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
     const int n = p.ccount[row];
     const V pi = load_pos(p, i);
     const int si = static_cast<int>(pi.w);
-    const T fpi = p.fp[i];
+    const T fpi = FORCES ? p.fp[i] : T(0);
     T fx = T(0), fy = T(0), fz = T(0);
-    if (n <= p.row_cap && !LJX_FORCE_PREFETCH) {
+    if (n <= p.row_cap) {
       const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
       for (int k = lane; k < n; k += kWarp) {
         const int j = crow[k];
-        eam_edge<T, MODE>(p, pi, si, fpi, j, load_pos(p, j),
-                          MODE != kGhost ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
-      }
-    } else if (n <= p.row_cap) {
-      const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
-      int jn = lane < n ? crow[lane] : 0;
-      V pn = lane < n ? load_pos(p, jn) : pi;
-      T fn = (MODE != kGhost && lane < n) ? __ldg(p.fp + jn) : T(0);
-      for (int k = lane; k < n; k += kWarp) {
-        const int j = jn;
-        const V pj = pn;
-        const T fpj = fn;
-        if (k + kWarp < n) {
-          jn = crow[k + kWarp];
-          pn = load_pos(p, jn);
-          if (MODE != kGhost) fn = __ldg(p.fp + jn);
-        }
-        eam_edge<T, MODE>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v);
+        eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, load_pos(p, j),
+                                  kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
       }
     } else {
       const double4 xi = load4(p.xd4 + i);
@@ -641,23 +626,25 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
         const int j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
         if (j >= p.max_atoms) continue;
         if (pack_keep(p, i, xi, j, load4(p.xd4 + j)))
-          eam_edge<T, MODE>(p, pi, si, fpi, j, load_pos(p, j),
-                            MODE != kGhost ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
+          eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, load_pos(p, j),
+                                    kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
       }
     }
-    fx = warp_sum(fx);
-    fy = warp_sum(fy);
-    fz = warp_sum(fz);
-    if (lane == 0 && i < p.nall) {
-      double *fi = p.f + 3 * i;
-      if (MODE == kRowsFull) {
-        fi[0] += p.scale * static_cast<double>(fx);
-        fi[1] += p.scale * static_cast<double>(fy);
-        fi[2] += p.scale * static_cast<double>(fz);
-      } else {
-        atomicAdd(fi + 0, p.scale * static_cast<double>(fx));
-        atomicAdd(fi + 1, p.scale * static_cast<double>(fy));
-        atomicAdd(fi + 2, p.scale * static_cast<double>(fz));
+    if constexpr (FORCES) {
+      fx = warp_sum(fx);
+      fy = warp_sum(fy);
+      fz = warp_sum(fz);
+      if (lane == 0 && i < p.nall) {
+        double *fi = p.f + 3 * i;
+        if (MODE == kRowsFull) {
+          fi[0] += p.scale * static_cast<double>(fx);
+          fi[1] += p.scale * static_cast<double>(fy);
+          fi[2] += p.scale * static_cast<double>(fz);
+        } else {
+          atomicAdd(fi + 0, p.scale * static_cast<double>(fx));
+          atomicAdd(fi + 1, p.scale * static_cast<double>(fy));
+          atomicAdd(fi + 2, p.scale * static_cast<double>(fz));
+        }
       }
     }
   }
@@ -671,8 +658,8 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
 }
 
 // LJ 12-6 in one pass over the LAMMPS list: examples/export_model.py:16-74 with the force-add
-// conventions of cpp/pair_jax_kokkos.cpp:176-225.
-template <typename T, int MODE>
+// conventions of cpp/pair_jax_kokkos.cpp:176-225. Without FORCES: the energy alone.
+template <typename T, int MODE, bool FORCES = true>
 __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
 {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -718,13 +705,14 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
       const T inv_r2 = p.lj_sigma_sq / r2;
       const T inv_r6 = inv_r2 * inv_r2 * inv_r2;
       const T u = p.lj_four_eps * (inv_r6 * inv_r6 - inv_r6);
+      e += static_cast<double>(ew * u);
+      if constexpr (!FORCES) continue;
       // dU/drij = 2 rij dU/d(r^2), dU/d(r^2) = -4 eps (6 a^6 - 3 a^3) / r^2, a = sigma^2/r^2.
       const T g = T(-2) * p.lj_four_eps * (T(6) * inv_r6 * inv_r6 - T(3) * inv_r6) / r2 * fw;
       const T ex = g * dx, ey = g * dy, ez = g * dz;
       fx += ex;
       fy += ey;
       fz += ez;
-      e += static_cast<double>(ew * u);
       v[0] -= vw * static_cast<double>(dx * ex);
       v[1] -= vw * static_cast<double>(dy * ey);
       v[2] -= vw * static_cast<double>(dz * ez);
@@ -737,19 +725,21 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
         atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
       }
     }
-    fx = warp_sum(fx);
-    fy = warp_sum(fy);
-    fz = warp_sum(fz);
-    if (lane == 0 && i < p.nall) {
-      double *fi = p.f + 3 * i;
-      if (!scatter) {
-        fi[0] += p.scale * static_cast<double>(fx);
-        fi[1] += p.scale * static_cast<double>(fy);
-        fi[2] += p.scale * static_cast<double>(fz);
-      } else {
-        atomicAdd(fi + 0, p.scale * static_cast<double>(fx));
-        atomicAdd(fi + 1, p.scale * static_cast<double>(fy));
-        atomicAdd(fi + 2, p.scale * static_cast<double>(fz));
+    if constexpr (FORCES) {
+      fx = warp_sum(fx);
+      fy = warp_sum(fy);
+      fz = warp_sum(fz);
+      if (lane == 0 && i < p.nall) {
+        double *fi = p.f + 3 * i;
+        if (!scatter) {
+          fi[0] += p.scale * static_cast<double>(fx);
+          fi[1] += p.scale * static_cast<double>(fy);
+          fi[2] += p.scale * static_cast<double>(fz);
+        } else {
+          atomicAdd(fi + 0, p.scale * static_cast<double>(fx));
+          atomicAdd(fi + 1, p.scale * static_cast<double>(fy));
+          atomicAdd(fi + 2, p.scale * static_cast<double>(fz));
+        }
       }
     }
     kept_sum += kept;

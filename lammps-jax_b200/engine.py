@@ -157,6 +157,10 @@ class Engine:
         self._check(self.lib.ljx_force(self._h, _stream(stream), ctypes.byref(atoms),
                                        ctypes.byref(nl), int(newton_pair), float(scale)))
 
+    def energy(self, atoms, nl, newton_pair, scale=1.0, stream=None):
+        self._check(self.lib.ljx_energy(self._h, _stream(stream), ctypes.byref(atoms),
+                                        ctypes.byref(nl), int(newton_pair), float(scale)))
+
     def read_result(self, stream=None) -> abi.Result:
         res = abi.Result()
         self._check(self.lib.ljx_read_result(self._h, _stream(stream), ctypes.byref(res)))
@@ -281,10 +285,19 @@ class PairJax:
     def init_one(self) -> float:
         return float(self.bundle.contract["cutoff"])
 
-    def compute(self, system: System, eflag: bool = True, vflag: bool = True, stream=None):
-        """One force evaluation; forces are added into system.f (ghost rows too, newton on)."""
+    def compute(self, system: System, eflag: bool = True, vflag: bool = True, stream=None, *,
+                eflag_atom: bool = False, vflag_atom: bool = False, eflag_only: bool = False):
+        """One force evaluation; forces are added into system.f (ghost rows too, newton on).
+
+        eflag_only is LAMMPS's energy-only request (MC moves): the energy alone, no forces or
+        virial (cpp/pair_jax_kokkos.cpp:997-1001). The bundle's potential block always provides
+        the energy, so the reference's energy-program check cannot fail here."""
         if not self.model_loaded or self.engine is None:
             raise LammpsError("LAMMPS-JAX runtime is not initialized")
+        if eflag_atom:
+            raise LammpsError("pair jax/kk does not support per-atom energy output")
+        if vflag_atom:
+            raise LammpsError("pair jax/kk does not support per-atom virial output")
         if system.list is None:
             raise LammpsError("LAMMPS-JAX requires a Kokkos device neighbor list")
         eng, plan = self.engine, self.plan
@@ -303,10 +316,13 @@ class PairJax:
                 rows, width, elem = eng.feature_rows(0)
                 system.comm.reverse(rows, width, elem, stream)
             eng.embed(atoms, stream)
-            if plan.forward_fp:
-                rows, width, elem = eng.feature_rows(1)
-                system.comm.forward(rows, width, elem, stream)
-            eng.force(atoms, nl, newton, self.scale, stream)
+            if eflag_only:
+                eng.energy(atoms, nl, newton, self.scale, stream)
+            else:
+                if plan.forward_fp:
+                    rows, width, elem = eng.feature_rows(1)
+                    system.comm.forward(rows, width, elem, stream)
+                eng.force(atoms, nl, newton, self.scale, stream)
             res = eng.read_result(stream)
         except abi.LjxError as err:
             raise LammpsError(f"LAMMPS-JAX compute failed: {err}") from err
@@ -318,9 +334,9 @@ class PairJax:
                     f"per atom, capacity {c['max_neighbors']}")
             raise LammpsError(f"LAMMPS-JAX edge capacity exceeded: global max {res.edge_count} "
                               f"edges, capacity {c['max_edges']}")
-        if eflag:
+        if eflag or eflag_only:
             self.eng_vdwl += res.energy
-        if vflag:
+        if vflag and not eflag_only:
             for k in range(6):
                 self.virial[k] += res.virial[k]
         self.last = res
