@@ -241,7 +241,7 @@ def run_ljx(args):
     traffic = profile_traffic(kname)
 
     e2e = None if args.skip_extras else run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows,
-                                                 width, elem, args, nall, world)
+                                                 width, elem, args, nall, world, decomp["lists"])
     value = world * nlocal * args.steps / elapsed
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -310,10 +310,11 @@ def setup_single(ljx, cells, precision):
     pair = ljx.PairJax()
     pair.coeff(system, "*", "*", str(path))
     pair.init_style(system)
-    system.list = ljx.synth.neighbor_list(x_all, nlocal, CUTOFF + SKIN, half=False)
+    builder = ljx.synth.DeviceListBuilder(x_all, nlocal, CUTOFF + SKIN, half=False)
+    system.list = builder.build(x)
     system.comm = ljx.SelfComm(torch.as_tensor(owner, device="cuda"), nlocal)
     return system, nlocal, nall, {"pair": pair, "parallelism": "single GPU (periodic self-images)",
-                                  "comm_launches": 1}
+                                  "comm_launches": 1, "lists": builder}
 
 
 def setup_decomposed(ljx, cells, rank, world, precision, local):
@@ -340,34 +341,31 @@ def setup_decomposed(ljx, cells, rank, world, precision, local):
     pair = ljx.PairJax(device=local)
     pair.coeff(system, "*", "*", str(path))
     pair.init_style(system)
-    system.list = ljx.synth.neighbor_list(slab.x, nlocal, CUTOFF + SKIN, half=False)
+    builder = ljx.synth.DeviceListBuilder(slab.x, nlocal, CUTOFF + SKIN, half=False)
+    system.list = builder.build(x)
     elem = 8 if precision == "float64" else 4
     system.comm = halo.SlabExchange(slab, 1, elem)
     return system, nlocal, nall, {
-        "pair": pair, "comm_launches": system.comm.launches_per_exchange,
+        "pair": pair, "comm_launches": system.comm.launches_per_exchange, "lists": builder,
         "parallelism": f"z-slab spatial decomposition over {world} GPUs, F'(rho) halo by "
                        "grouped NCCL send/recv with both z-neighbors + x/y periodic images",
         "close": lambda: None}
 
 
-def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall, world):
-    """Same step through the C ABI with host buffers: H2D of x every step and of the neighbor
-    list every 10th step (the C3 rebuild period), D2H of forces and the result every step."""
+def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall, world, lists):
+    """Same step through the C ABI with host buffers: H2D of x and D2H of the forces and the
+    result every step. Every 10th step (the C3 rebuild period) the neighbor list is rebuilt on
+    the device from the uploaded positions (ljx_neigh_bin + ljx_neigh_build into the same
+    buffers), as LAMMPS-Kokkos builds it on the device."""
     x_host = system.x.cpu().pin_memory()
     f_host = torch.empty_like(system.f, device="cpu").pin_memory()
-    nb = system.list.neighbors
-    nb_host = nb.cpu().pin_memory()
-    nn_host = system.list.numneigh.cpu().pin_memory()
     stream = torch.cuda.current_stream()
     steps = max(3, min(args.steps, 10))
 
     def one(k):
         system.x.copy_(x_host, non_blocking=True)
-        h2d = x_host.numel() * 8
         if k % 10 == 0:
-            nb.copy_(nb_host, non_blocking=True)
-            system.list.numneigh.copy_(nn_host, non_blocking=True)
-            h2d += nb_host.numel() * 4 + nn_host.numel() * 4
+            lists.launch(system.x, stream)
         nl.ago = k % 10 if args.rebuild_every > 0 else -1
         eng.pack_atoms(atoms)
         eng.density(atoms, nl, False)
@@ -376,11 +374,10 @@ def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall
         eng.force(atoms, nl, False, 1.0)
         f_host.copy_(system.f, non_blocking=True)
         eng.read_result()  # synchronizes the stream: forces and energy are on the host
-        return h2d
+        return x_host.numel() * 8
 
     one(1)
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     h2d = 0
@@ -389,10 +386,10 @@ def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall
     stop.record(stream)
     torch.cuda.synchronize()
     elapsed = start.elapsed_time(stop) / 1e3
-    del t0
     value = world * system.nlocal * steps / elapsed
     return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d / steps,
-            "d2h_bytes_per_step": f_host.numel() * 8 + 9 * 8, "steps": steps}
+            "d2h_bytes_per_step": f_host.numel() * 8 + 9 * 8, "steps": steps,
+            "list": "rebuilt on the device every 10th step from the uploaded positions"}
 
 
 def cpu_baseline(args, sample_cells=(40, 40, 40), steps=None):

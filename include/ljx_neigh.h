@@ -7,7 +7,7 @@
  * Binning: atoms are pre-sorted into a uniform grid of cubic bins (side `binsize` >= cutoff/2,
  * origin `lo`, `nbins` per dimension); bin b holds bin_atoms[bin_start[b] .. bin_start[b+1]).
  * `lo` (3 doubles) and `nbins` (3 ints) are HOST arrays; every other pointer is device memory.
- * Each owned atom scans a +-2 bin stencil. half != 0 keeps each pair once: owned j > i, or a
+ * Each owned atom scans the bins of a +-2 stencil whose box lies within the cutoff. half != 0 keeps each pair once: owned j > i, or a
  * ghost j whose (z, y, x) sorts after atom i's — the one-rank-per-pair rule of the reference
  * packer (cpp/pair_jax_kokkos.cpp:94-101).
  *
@@ -22,6 +22,15 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+
+/* Device binning for ljx_neigh_build (no counterpart in the reference: LAMMPS bins inside
+ * NPairKokkos): counting sort of the nall atoms of x into the grid given by lo, binsize and nbins
+ * (HOST arrays), atoms in index order within each bin. bin_start receives nbins_total + 1 ints,
+ * bin_atoms nall ints; scratch must hold nbins_total + ceil(nbins_total / 1024) ints. All three
+ * are device memory owned by the caller; nothing is allocated. */
+ljx_status ljx_neigh_bin(void *stream, const double *x, int nall, const double *lo,
+                         double binsize, const int *nbins, int *bin_start, int *bin_atoms,
+                         int *scratch);
 
 ljx_status ljx_neigh_build(void *stream, const double *x, int nall, int nlocal, double cutoff,
                            int half, const double *lo, double binsize, const int *nbins,

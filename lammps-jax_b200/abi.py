@@ -102,6 +102,8 @@ SIGNATURES = [
                                      c_void_p]),
     ("ljx_engine_launches", c_longlong, [c_void_p]),
     ("ljx_version", c_char_p, []),
+    ("ljx_neigh_bin", c_int, [c_void_p, c_void_p, c_int, c_void_p, c_double, c_void_p,
+                              c_void_p, c_void_p, c_void_p]),
     ("ljx_neigh_build", c_int, [c_void_p, c_void_p, c_int, c_int, c_double, c_int, c_void_p,
                                 c_double, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong,
                                 c_int, c_void_p, c_void_p]),

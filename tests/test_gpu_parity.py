@@ -74,6 +74,20 @@ def test_neighbor_list_matches_oracle(oracle):
             np.testing.assert_array_equal(mine, theirs)
 
 
+def test_device_binning_matches_host():
+    """ljx_neigh_bin's counting sort equals the host binning: same bin starts, and atoms in
+    index order within each bin."""
+    ljx = load_package()
+    case = eam_case(cells=(5, 5, 5), seed=19, nr=500, nrho=500)
+    cut = case.cutoff + case.skin
+    builder = ljx.synth.DeviceListBuilder(case.x_all, case.nlocal, cut)
+    builder.launch(torch.as_tensor(case.x_all, device="cuda"))
+    torch.cuda.synchronize()
+    lo, binsize, nb, start, order = ljx.synth.bin_atoms(case.x_all, cut)
+    np.testing.assert_array_equal(builder.bin_start.cpu().numpy(), start)
+    np.testing.assert_array_equal(builder.bin_atoms.cpu().numpy(), order)
+
+
 @pytest.mark.parametrize("mode", ["rows-full", "ghost", "half-unique"])
 def test_pack_edges_bit_exact(tmp_path, oracle, mode):
     ljx = load_package()
