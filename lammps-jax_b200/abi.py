@@ -55,6 +55,18 @@ class Result(Structure):
                 ("overflow", c_int), ("widest_row", c_int)]
 
 
+COMM_FN = ctypes.CFUNCTYPE(c_int, c_void_p, c_void_p, c_int, c_int, c_void_p)
+REDUCE_FN = ctypes.CFUNCTYPE(c_int, c_void_p, POINTER(c_int), c_int)
+
+
+class PairHost(Structure):
+    _fields_ = [("ctx", c_void_p), ("forward_comm", COMM_FN), ("reverse_comm", COMM_FN),
+                ("allreduce_max", REDUCE_FN)]
+
+
+EFLAG_GLOBAL, VFLAG_GLOBAL, EFLAG_ATOM, VFLAG_ATOM, EFLAG_ONLY = 1, 2, 4, 8, 16
+
+
 class Plan(Structure):
     _fields_ = [("half_list", c_int), ("reverse_density", c_int), ("forward_fp", c_int),
                 ("reverse_force", c_int), ("comm_width", c_int), ("comm_elem_bytes", c_int)]
@@ -101,6 +113,19 @@ SIGNATURES = [
                                      c_double, c_double, c_int, c_int, c_int, c_double,
                                      c_void_p]),
     ("ljx_engine_launches", c_longlong, [c_void_p]),
+    ("ljx_pair_create", c_int, [c_int, POINTER(c_void_p)]),
+    ("ljx_pair_destroy", None, [c_void_p]),
+    ("ljx_pair_error", c_char_p, [c_void_p]),
+    ("ljx_pair_settings", c_int, [c_void_p, c_int, POINTER(c_char_p)]),
+    ("ljx_pair_coeff", c_int, [c_void_p, c_int, POINTER(c_char_p), c_char_p, c_int]),
+    ("ljx_pair_init_style", c_int, [c_void_p, c_int, c_int, POINTER(c_double), POINTER(c_double),
+                                    c_int, POINTER(c_char_p), POINTER(Plan)]),
+    ("ljx_pair_init_one", c_double, [c_void_p]),
+    ("ljx_pair_compute", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
+                                 c_int, POINTER(PairHost), POINTER(Result)]),
+    ("ljx_pair_tally", c_int, [c_void_p, POINTER(c_double), POINTER(c_double)]),
+    ("ljx_pair_bundle", c_void_p, [c_void_p]),
+    ("ljx_pair_engine", c_void_p, [c_void_p]),
     ("ljx_version", c_char_p, []),
     ("ljx_neigh_bin", c_int, [c_void_p, c_void_p, c_int, c_void_p, c_double, c_void_p,
                               c_void_p, c_void_p, c_void_p]),

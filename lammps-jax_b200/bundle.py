@@ -103,9 +103,10 @@ def _decode(value) -> str:
 class Bundle:
     """A bundle parsed and validated by the library's loader (ljx_bundle_load)."""
 
-    def __init__(self, handle: int):
+    def __init__(self, handle: int, owned: bool = True):
         self._handle = ctypes.c_void_p(handle)
         self._lib = abi.load()
+        self._owned = owned
 
     @classmethod
     def load(cls, path) -> "Bundle":
@@ -174,7 +175,7 @@ class Bundle:
 
     def __del__(self):
         try:
-            if self._handle:
+            if self._handle and self._owned:
                 self._lib.ljx_bundle_free(self._handle)
                 self._handle = ctypes.c_void_p()
         except Exception:

@@ -1,9 +1,10 @@
-"""Host side of the drop-in: the engine handle and a mirror of PairJaxKokkos.
+"""Host side of the drop-in for the harness and the tests: handles on the engine and on the pair
+style.
 
-`PairJax` follows cpp/pair_jax_kokkos.cpp — settings (:573-580), coeff (:582-663), init_style
-(:665-785), init_one (:787-792) and compute (:989-1102) — with the same arguments, the same
-checks and the same error messages, but every array operation goes to libljx through its C ABI
-on a CUDA stream. torch supplies device memory and streams only.
+`PairJax` drives libljx's pair style (include/ljx_pair.h, csrc/pair.cpp), the C++ restatement of
+cpp/pair_jax_kokkos.cpp — settings (:573-580), coeff (:582-663), init_style (:665-785), init_one
+(:787-792) and compute (:989-1102) — with the same arguments, checks and error messages. Every
+array operation runs in libljx on a CUDA stream; torch supplies device memory and streams only.
 
 `System` stands in for the LAMMPS state the pair style reads (x, type, f, nlocal, nghost, the
 neighbor list) and `SelfComm` for LAMMPS's comm on one rank whose ghosts are periodic images.
@@ -70,6 +71,9 @@ class System:
     list: NeighborList | None = None
     comm: object = None
     fixes: builtins.list = field(default_factory=builtins.list)
+    molecular: bool = False
+    special_lj: tuple = (1.0, 1.0, 1.0, 1.0)     # force->special_lj[0..3]
+    special_coul: tuple = (1.0, 1.0, 1.0, 1.0)   # force->special_coul[0..3]
 
     @property
     def nall(self) -> int:
@@ -112,14 +116,20 @@ class SelfComm:
 class Engine:
     """One ljx_engine: device buffers sized from the bundle contract."""
 
-    def __init__(self, bundle: Bundle, device: int = 0):
+    def __init__(self, bundle: Bundle, device: int = 0, handle: int | None = None):
+        """A new engine for `bundle`, or (handle given) a view of an engine someone else owns,
+        such as the one behind a PairJax."""
         self.lib = abi.load()
         self.bundle = bundle
-        out = ctypes.c_void_p()
-        status = self.lib.ljx_engine_create(bundle.handle, device, ctypes.byref(out))
-        if status != abi.OK:
-            raise abi.LjxError(status, self.lib.ljx_bundle_error().decode())
-        self._h = out
+        self._owned = handle is None
+        if handle is None:
+            out = ctypes.c_void_p()
+            status = self.lib.ljx_engine_create(bundle.handle, device, ctypes.byref(out))
+            if status != abi.OK:
+                raise abi.LjxError(status, self.lib.ljx_bundle_error().decode())
+            self._h = out
+        else:
+            self._h = ctypes.c_void_p(handle)
         self.contract = bundle.contract
         self.f64 = self.contract["precision"] == abi.FLOAT64
 
@@ -187,9 +197,9 @@ class Engine:
         return int(self.lib.ljx_engine_launches(self._h))
 
     def close(self):
-        if getattr(self, "_h", None):
+        if getattr(self, "_h", None) and getattr(self, "_owned", True):
             self.lib.ljx_engine_destroy(self._h)
-            self._h = None
+        self._h = None
 
     def __del__(self):
         try:
@@ -221,123 +231,141 @@ def _cuda_memcpy_dtod(dst: int, src: int, nbytes: int):
 
 
 class PairJax:
-    """pair_style jax/kk on the ljx engine (mirror of PairJaxKokkos)."""
-
-    PLATFORM = "cuda"
+    """pair_style jax/kk: a handle on libljx's pair style (include/ljx_pair.h), the C++ restatement
+    of PairJaxKokkos. The methods take the LAMMPS state from a `System`; checks, their order and
+    messages are the library's (the reference's). `system.comm` serves the exchanges."""
 
     def __init__(self, device: int = 0):
+        self.lib = abi.load()
         self.device = device
-        self.scale = 1.0
+        out = ctypes.c_void_p()
+        if self.lib.ljx_pair_create(device, ctypes.byref(out)) != abi.OK:
+            raise LammpsError("Failed to create pair jax/kk")
+        self._h = out
         self.bundle: Bundle | None = None
         self.engine: Engine | None = None
-        self.model_loaded = False
         self.plan: abi.Plan | None = None
-        self.eng_vdwl = 0.0
-        self.virial = [0.0] * 6
         self.last = None
 
+    def _check(self, status: int):
+        if status != abi.OK:
+            raise LammpsError(self.lib.ljx_pair_error(self._h).decode())
+
+    @staticmethod
+    def _argv(args):
+        raw = [str(a).encode() for a in args]
+        return len(raw), (ctypes.c_char_p * max(1, len(raw)))(*raw)
+
     def settings(self, *args):
-        # pair_style jax/kk [plugin-path]: the path is accepted and ignored (no PJRT plugin).
-        if len(args) > 1:
-            raise LammpsError("Illegal pair_style jax/kk command")
+        n, argv = self._argv(args)
+        self._check(self.lib.ljx_pair_settings(self._h, n, argv))
 
     def coeff(self, system: System, *args):
-        if len(args) < 3 or len(args) > 4:
-            raise LammpsError("Illegal pair_coeff jax/kk command")
-        if len(args) == 4:
-            self.scale = float(args[3])
-        try:
-            self.bundle = Bundle.load(args[2])
-        except abi.LjxError as err:
-            raise LammpsError(f"Failed to load LAMMPS-JAX model: {err}") from err
-        c = self.bundle.contract
-        if c["unit_style"] != system.unit_style:
-            raise LammpsError("LAMMPS-JAX model unit style does not match current units")
-        if c["n_species"] > 0 and system.ntypes > c["n_species"]:
-            raise LammpsError(
-                f"LAMMPS-JAX model distinguishes {c['n_species']} species but the system defines "
-                f"{system.ntypes} atom types; types beyond the model's range would silently map "
-                "to its last species")
-        if c["platform"] != self.PLATFORM:
-            raise LammpsError(
-                f"LAMMPS-JAX model was exported for {c['platform']} but this build runs "
-                f"{self.PLATFORM}; re-export it with platform=\"{self.PLATFORM}\"")
-        try:
-            self.engine = Engine(self.bundle, self.device)
-        except abi.LjxError as err:
-            raise LammpsError(f"Failed to initialize LAMMPS-JAX runtime: {err}") from err
-        self.model_loaded = True
+        self.engine = None
+        n, argv = self._argv(args)
+        status = self.lib.ljx_pair_coeff(self._h, n, argv, system.unit_style.encode(),
+                                         system.ntypes)
+        handle = self.lib.ljx_pair_bundle(self._h)
+        self.bundle = Bundle(handle, owned=False) if handle else None
+        eng = self.lib.ljx_pair_engine(self._h)
+        if eng:
+            self.engine = Engine(self.bundle, self.device, handle=eng)
+        self._check(status)
+
+    @property
+    def model_loaded(self) -> bool:
+        return self.engine is not None
 
     def init_style(self, system: System):
-        if not self.model_loaded:
-            raise LammpsError("LAMMPS-JAX model has not been loaded")
-        for fix in system.fixes:
-            if not system.newton_pair and any(k in fix for k in ("npt", "nph", "press",
-                                                                 "box/relax", "msst")):
-                raise LammpsError(f"Fix {fix} requires pair virial; run pair jax/kk with newton "
-                                  "pair on")
-        try:
-            self.plan = self.engine.plan(system.newton_pair)
-        except abi.LjxError as err:
-            raise LammpsError(str(err)) from err
-        return {"half_list": bool(self.plan.half_list)}
+        fixes = [str(f).encode() for f in system.fixes]
+        arr = (ctypes.c_char_p * max(1, len(fixes)))(*fixes)
+        lj = (ctypes.c_double * 4)(*system.special_lj)
+        coul = (ctypes.c_double * 4)(*system.special_coul)
+        plan = abi.Plan()
+        self._check(self.lib.ljx_pair_init_style(self._h, int(system.newton_pair),
+                                                 int(system.molecular), lj, coul, len(fixes), arr,
+                                                 ctypes.byref(plan)))
+        self.plan = plan
+        return {"half_list": bool(plan.half_list)}
 
     def init_one(self) -> float:
-        return float(self.bundle.contract["cutoff"])
+        return float(self.lib.ljx_pair_init_one(self._h))
 
     def compute(self, system: System, eflag: bool = True, vflag: bool = True, stream=None, *,
                 eflag_atom: bool = False, vflag_atom: bool = False, eflag_only: bool = False):
         """One force evaluation; forces are added into system.f (ghost rows too, newton on).
-
-        eflag_only is LAMMPS's energy-only request (MC moves): the energy alone, no forces or
-        virial (cpp/pair_jax_kokkos.cpp:997-1001). The bundle's potential block always provides
-        the energy, so the reference's energy-program check cannot fail here."""
-        if not self.model_loaded or self.engine is None:
-            raise LammpsError("LAMMPS-JAX runtime is not initialized")
-        if eflag_atom:
-            raise LammpsError("pair jax/kk does not support per-atom energy output")
-        if vflag_atom:
-            raise LammpsError("pair jax/kk does not support per-atom virial output")
+        eflag_only is LAMMPS's energy-only request (MC moves): the energy alone."""
         if system.list is None:
             raise LammpsError("LAMMPS-JAX requires a Kokkos device neighbor list")
-        eng, plan = self.engine, self.plan
+        flags = ((abi.EFLAG_GLOBAL if eflag else 0) | (abi.VFLAG_GLOBAL if vflag else 0) |
+                 (abi.EFLAG_ATOM if eflag_atom else 0) | (abi.VFLAG_ATOM if vflag_atom else 0) |
+                 (abi.EFLAG_ONLY if eflag_only else 0))
+        comm = system.comm
+        failures = []
+
+        def forward(_ctx, rows, width, elem, strm):
+            try:
+                comm.forward(rows, width, elem, stream)
+                return 0
+            except Exception as err:  # reported through the pair style's status
+                failures.append(err)
+                return 1
+
+        def reverse(_ctx, rows, width, elem, strm):
+            try:
+                comm.reverse(rows, width, elem, stream)
+                return 0
+            except Exception as err:
+                failures.append(err)
+                return 1
+
+        def reduce(_ctx, values, n):
+            try:
+                if hasattr(comm, "allreduce_max"):
+                    out = comm.allreduce_max([values[k] for k in range(n)])
+                    for k in range(n):
+                        values[k] = int(out[k])
+                return 0
+            except Exception as err:
+                failures.append(err)
+                return 1
+
+        host = abi.PairHost(None, abi.COMM_FN(forward), abi.COMM_FN(reverse),
+                            abi.REDUCE_FN(reduce))
+        res = abi.Result()
         atoms = system.atoms()
         nl = system.list.struct()
-        newton = system.newton_pair
-        try:
-            eng.pack_atoms(atoms, stream)
-        except abi.LjxError as err:
-            if err.status == abi.ERR_CAPACITY:
-                raise LammpsError(str(err)) from err
-            raise LammpsError(f"LAMMPS-JAX compute failed: {err}") from err
-        try:
-            eng.density(atoms, nl, newton, stream)
-            if plan.reverse_density:
-                rows, width, elem = eng.feature_rows(0)
-                system.comm.reverse(rows, width, elem, stream)
-            eng.embed(atoms, stream)
-            if eflag_only:
-                eng.energy(atoms, nl, newton, self.scale, stream)
-            else:
-                if plan.forward_fp:
-                    rows, width, elem = eng.feature_rows(1)
-                    system.comm.forward(rows, width, elem, stream)
-                eng.force(atoms, nl, newton, self.scale, stream)
-            res = eng.read_result(stream)
-        except abi.LjxError as err:
-            raise LammpsError(f"LAMMPS-JAX compute failed: {err}") from err
-        c = self.bundle.contract
-        if res.overflow:
-            if c["input_layout"] == abi.LAYOUT_NEIGHBOR_MATRIX:
-                raise LammpsError(
-                    f"LAMMPS-JAX neighbor capacity exceeded: global max {res.widest_row} neighbors "
-                    f"per atom, capacity {c['max_neighbors']}")
-            raise LammpsError(f"LAMMPS-JAX edge capacity exceeded: global max {res.edge_count} "
-                              f"edges, capacity {c['max_edges']}")
-        if eflag or eflag_only:
-            self.eng_vdwl += res.energy
-        if vflag and not eflag_only:
-            for k in range(6):
-                self.virial[k] += res.virial[k]
+        status = self.lib.ljx_pair_compute(self._h, _stream(stream), ctypes.byref(atoms),
+                                           ctypes.byref(nl), int(system.newton_pair), flags,
+                                           ctypes.byref(host), ctypes.byref(res))
+        if status != abi.OK and failures:
+            raise LammpsError(f"{self.lib.ljx_pair_error(self._h).decode()} ({failures[0]})")
+        self._check(status)
         self.last = res
         return res
+
+    def _tally(self):
+        e = ctypes.c_double()
+        v = (ctypes.c_double * 6)()
+        self.lib.ljx_pair_tally(self._h, ctypes.byref(e), v)
+        return e.value, list(v)
+
+    @property
+    def eng_vdwl(self) -> float:
+        return self._tally()[0]
+
+    @property
+    def virial(self) -> list:
+        return self._tally()[1]
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.engine = None
+            self.lib.ljx_pair_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
