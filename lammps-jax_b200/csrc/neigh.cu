@@ -1,8 +1,10 @@
-// Device neighbor-list build for the harness: one thread per owned atom scans a +-2 stencil of
-// bins (bin side >= cutoff / 2) and writes its row in Kokkos LayoutLeft, so a warp's 32 rows
-// store each slot as one coalesced 128-byte line.
+// Device neighbor-list build for the harness: bins of side >= cutoff / 2 (counting sort on the
+// device, ljx_neigh_bin), then one warp per bin scans the +-2 stencil (ljx_neigh_build) and
+// writes the bin's rows in Kokkos LayoutLeft.
 
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "ljx_neigh.h"
 
@@ -99,70 +101,133 @@ __global__ void k_bin_order(const int *__restrict__ start, long long nb, int *bi
   }
 }
 
-__global__ void k_neigh_build(const double *__restrict__ x, int nlocal, double cutsq, int half,
-                              Grid g, const int *__restrict__ bin_start,
-                              const int *__restrict__ bin_atoms, int *__restrict__ neighbors,
-                              long long stride, int maxneigh, int *__restrict__ numneigh,
-                              int *__restrict__ widest)
+// One warp per bin: the bin's owned atoms (in index order, up to kRowsPerPass at a time) are
+// the rows; the atoms of the +-2 stencil are the candidates. For each (dy, dz) the five bins
+// along x are consecutive, so their atoms form one range of bin_atoms that the lanes read 32 at
+// a time; each candidate is tested against every row (row positions are shared-memory
+// broadcasts). Kept neighbors append to the rows in shared memory in stencil order; slots past
+// kRowCap go straight to global memory. The rows then leave slot-major, so one store covers the
+// same slot of consecutive rows (LayoutLeft).
+constexpr int kRowsPerPass = 8;
+constexpr int kRowCap = 256;
+constexpr int kNeighWarps = 4;
+
+__global__ void __launch_bounds__(kNeighWarps * 32)
+k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, Grid g,
+             const int *__restrict__ bin_start, const int *__restrict__ bin_atoms,
+             int *__restrict__ neighbors, long long stride, int maxneigh,
+             int *__restrict__ numneigh, int *__restrict__ widest)
 {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nlocal) return;
-  const double xi = x[3 * i], yi = x[3 * i + 1], zi = x[3 * i + 2];
-  int c[3];
-  const double xyz[3] = {xi, yi, zi};
-  for (int k = 0; k < 3; ++k) {
-    int v = static_cast<int>(floor((xyz[k] - g.lo[k]) * g.inv_bin));
-    c[k] = v < 0 ? 0 : (v >= g.nb[k] ? g.nb[k] - 1 : v);
-  }
-  // Distance from the atom to the near face of bin b along one axis (0 inside the slab).
-  auto gap = [&](int k, int b) {
-    const double blo = g.lo[k] + b * g.bin, bhi = blo + g.bin;
-    const double v = xyz[k];
-    return v < blo ? blo - v : (v > bhi ? v - bhi : 0.0);
-  };
-  int n = 0;
-  for (int dz = -2; dz <= 2; ++dz) {
-    const int bz = c[2] + dz;
-    if (bz < 0 || bz >= g.nb[2]) continue;
-    const double gz = gap(2, bz);
-    for (int dy = -2; dy <= 2; ++dy) {
-      const int by = c[1] + dy;
-      if (by < 0 || by >= g.nb[1]) continue;
-      const double gy = gap(1, by);
-      for (int dx = -2; dx <= 2; ++dx) {
-        const int bx = c[0] + dx;
-        if (bx < 0 || bx >= g.nb[0]) continue;
-        // Bins whose box lies beyond the cutoff hold no neighbor (a little slack keeps the
-        // pruning conservative against rounding).
-        const double gx = gap(0, bx);
-        if (gx * gx + gy * gy + gz * gz > cutsq * (1.0 + 1e-9)) continue;
-        const long long b = (static_cast<long long>(bz) * g.nb[1] + by) * g.nb[0] + bx;
-        const int end = bin_start[b + 1];
-        for (int s = bin_start[b]; s < end; ++s) {
-          const int j = bin_atoms[s];
-          if (j == i) continue;
-          const double xj = x[3 * j], yj = x[3 * j + 1], zj = x[3 * j + 2];
-          const double ex = xi - xj, ey = yi - yj, ez = zi - zj;
-          if (ex * ex + ey * ey + ez * ez >= cutsq) continue;
-          if (half) {
-            if (j < nlocal) {
-              if (j < i) continue;
-            } else {
-              if (zj < zi) continue;
-              if (zj == zi) {
-                if (yj < yi) continue;
-                if (yj == yi && xj < xi) continue;
+  __shared__ int s_row[kNeighWarps][kRowsPerPass][kRowCap];
+  __shared__ double s_xi[kNeighWarps][kRowsPerPass][3];
+  __shared__ int s_i[kNeighWarps][kRowsPerPass];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  const long long nbins = static_cast<long long>(g.nb[0]) * g.nb[1] * g.nb[2];
+  int (*rows)[kRowCap] = s_row[warp];
+  double (*xis)[3] = s_xi[warp];
+  int *is = s_i[warp];
+  int wide = 0;
+  for (long long b = static_cast<long long>(blockIdx.x) * kNeighWarps + warp; b < nbins;
+       b += static_cast<long long>(gridDim.x) * kNeighWarps) {
+    const int b0 = bin_start[b], b1 = bin_start[b + 1];
+    // Owned atoms come first within a bin (index order).
+    int owned = 0;
+    for (int s0 = b0; s0 < b1; s0 += 32) {
+      const bool own = s0 + lane < b1 && bin_atoms[s0 + lane] < nlocal;
+      owned += __popc(__ballot_sync(0xffffffffu, own));
+    }
+    if (owned == 0) continue;
+    const int bz = static_cast<int>(b / (static_cast<long long>(g.nb[0]) * g.nb[1]));
+    const int by = static_cast<int>((b / g.nb[0]) % g.nb[1]);
+    const int bx = static_cast<int>(b % g.nb[0]);
+    for (int r0 = 0; r0 < owned; r0 += kRowsPerPass) {
+      const int m = min(kRowsPerPass, owned - r0);
+      if (lane < m) {
+        const int i = bin_atoms[b0 + r0 + lane];
+        is[lane] = i;
+        xis[lane][0] = x[3 * i];
+        xis[lane][1] = x[3 * i + 1];
+        xis[lane][2] = x[3 * i + 2];
+      }
+      __syncwarp();
+      int count[kRowsPerPass] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int dz = -2; dz <= 2; ++dz) {
+        const int cz = bz + dz;
+        if (cz < 0 || cz >= g.nb[2]) continue;
+        for (int dy = -2; dy <= 2; ++dy) {
+          const int cy = by + dy;
+          if (cy < 0 || cy >= g.nb[1]) continue;
+          // Bins wider than cutoff / 2 can put a whole (dy, dz) row of bins out of range.
+          const double gy = (dy > 1 ? dy - 1 : (dy < -1 ? -dy - 1 : 0)) * g.bin;
+          const double gz = (dz > 1 ? dz - 1 : (dz < -1 ? -dz - 1 : 0)) * g.bin;
+          if (gy * gy + gz * gz > cutsq * (1.0 + 1e-9)) continue;
+          // The bins bx-2 .. bx+2 of this row are consecutive, so their atoms are one range.
+          const long long row0 = (static_cast<long long>(cz) * g.nb[1] + cy) * g.nb[0];
+          const int c0 = bin_start[row0 + max(bx - 2, 0)];
+          const int c1 = bin_start[row0 + min(bx + 2, g.nb[0] - 1) + 1];
+          for (int s0 = c0; s0 < c1; s0 += 32) {
+            int j = -1;
+            double xj = 0, yj = 0, zj = 0;
+            if (s0 + lane < c1) {
+              j = bin_atoms[s0 + lane];
+              xj = x[3 * j];
+              yj = x[3 * j + 1];
+              zj = x[3 * j + 2];
+            }
+#pragma unroll
+            for (int r = 0; r < kRowsPerPass; ++r) {
+              if (r >= m) continue;  // m is the same for every lane
+              const int i = is[r];
+              const double ex = xis[r][0] - xj, ey = xis[r][1] - yj, ez = xis[r][2] - zj;
+              bool keep = j >= 0 && j != i && ex * ex + ey * ey + ez * ez < cutsq;
+              if (keep && half) {
+                if (j < nlocal) {
+                  keep = j > i;
+                } else {
+                  const double zi = xis[r][2], yi = xis[r][1], xi = xis[r][0];
+                  keep = !(zj < zi || (zj == zi && (yj < yi || (yj == yi && xj < xi))));
+                }
               }
+              const unsigned mk = __ballot_sync(0xffffffffu, keep);
+              if (keep) {
+                const int slot = count[r] + __popc(mk & below);
+                if (slot < kRowCap)
+                  rows[r][slot] = j;
+                else if (slot < maxneigh)
+                  neighbors[i + static_cast<long long>(slot) * stride] = j;
+              }
+              count[r] += __popc(mk);
             }
           }
-          if (n < maxneigh) neighbors[i + static_cast<long long>(n) * stride] = j;
-          ++n;
         }
       }
+      __syncwarp();
+      // Slot-major write-out: lane l takes row l % 8 at slot n + l / 8.
+      int longest = 0;
+#pragma unroll
+      for (int r = 0; r < kRowsPerPass; ++r) longest = max(longest, r < m ? count[r] : 0);
+      const int r = lane % kRowsPerPass;
+      int mine = 0;
+#pragma unroll
+      for (int rr = 0; rr < kRowsPerPass; ++rr)
+        if (rr == r && rr < m) mine = count[rr];
+      const int stop = min(min(longest, kRowCap), maxneigh);
+      for (int n0 = 0; n0 < stop; n0 += 32 / kRowsPerPass) {
+        const int n = n0 + lane / kRowsPerPass;
+        if (r < m && n < mine && n < stop)
+          neighbors[is[r] + static_cast<long long>(n) * stride] = rows[r][n];
+      }
+      if (lane < m) {
+        numneigh[is[lane]] = min(mine, maxneigh);
+        wide = max(wide, mine);
+      }
+      __syncwarp();
     }
   }
-  numneigh[i] = n < maxneigh ? n : maxneigh;
-  atomicMax(widest, n);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wide = max(wide, __shfl_xor_sync(0xffffffffu, wide, o));
+  if (lane == 0 && wide > 0) atomicMax(widest, wide);
 }
 
 }  // namespace
@@ -189,9 +254,11 @@ extern "C" ljx_status ljx_neigh_build(void *stream, const double *x, int nall, i
   g.inv_bin = 1.0 / binsize;
   auto s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(widest, 0, sizeof(int), s) != cudaSuccess) return LJX_ERR_CUDA;
-  k_neigh_build<<<(nlocal + 127) / 128, 128, 0, s>>>(x, nlocal, cutoff * cutoff, half, g,
-                                                     bin_start, bin_atoms, neighbors, slot_stride,
-                                                     maxneigh, numneigh, widest);
+  const long long nb = static_cast<long long>(g.nb[0]) * g.nb[1] * g.nb[2];
+  const long long blocks = std::min<long long>((nb + kNeighWarps - 1) / kNeighWarps, 148LL * 64);
+  k_neigh_bins<<<static_cast<unsigned>(blocks), kNeighWarps * 32, 0, s>>>(
+      x, nlocal, cutoff * cutoff, half, g, bin_start, bin_atoms, neighbors, slot_stride, maxneigh,
+      numneigh, widest);
   return cudaGetLastError() == cudaSuccess ? LJX_OK : LJX_ERR_CUDA;
 }
 
