@@ -12,9 +12,10 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden"
-# The reference checkout is only present in the build container; tests that need its data
-# files (the CuZr table) skip elsewhere.
-REFERENCE = Path(os.environ.get("LJX_REFERENCE", "/root/reference"))
+# The reference checkout (a directory named reference beside this repository, or LJX_REFERENCE)
+# is only present where the fixtures were made; tests that need its data files (the CuZr table)
+# skip elsewhere.
+REFERENCE = Path(os.environ.get("LJX_REFERENCE", ROOT.parent / "reference"))
 CUZR_TABLE = REFERENCE / "examples" / "potentials" / "CuZr.eam.alloy.gz"
 
 sys.path.insert(0, str(ROOT / "oracle"))

@@ -1,7 +1,7 @@
 """Generate the golden vectors in tests/golden/ by running the lammps-jax reference itself.
 
-Run in a container where the reference checkout exists (default /root/reference, override with
-LJX_REFERENCE):  python tests/golden/make_golden.py
+Run where the reference checkout exists (a directory named reference beside this repository, or
+the path in LJX_REFERENCE):  python tests/golden/make_golden.py
 
 jax is not installed here, so numpy_jax_shim.py stands in for jax.numpy; the reference's own
 python/lammps_jax/eam.py and the LJ energy builder of examples/export_model.py then run
@@ -32,7 +32,7 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("LJX_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("LJX_REFERENCE", HERE.parents[2] / "reference"))
 
 sys.path.insert(0, str(HERE))
 import numpy_jax_shim  # noqa: E402
