@@ -1,7 +1,8 @@
 // ljx engine: the extern "C" layer of include/ljx.h. Replaces the reference's PJRT runtime
 // (cpp/pjrt/runtime.{h,cpp}) and the Kokkos pack/add/virial/comm functors of
-// cpp/pair_jax_kokkos.cpp with hand-written sm_100a kernels (kernels.cuh). Buffers are sized
-// once from the bundle contract; no call allocates or synchronizes except ljx_read_result.
+// cpp/pair_jax_kokkos.cpp with hand-written sm_100a kernels (kernels.cuh, and groups.cuh for the
+// row-group candidate cache). Buffers are sized once from the bundle contract; no call allocates
+// or synchronizes except ljx_read_result.
 
 #include <cuda_runtime.h>
 
@@ -10,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -36,15 +38,19 @@ void check(cudaError_t err, const char *what)
     throw CudaError(std::string(what) + ": " + cudaGetErrorString(err));
 }
 
+// Resident blocks per SM of `kernel` at `block` threads (at most 8), computed once per kernel.
+// Engines on several host threads share the cache, hence the lock.
 template <typename Kernel>
-int blocks_per_sm(Kernel kernel)
+int blocks_per_sm(Kernel kernel, int block = ljx::kBlock)
 {
+  static std::mutex lock;
   static std::unordered_map<const void *, int> cache;
   const void *key = reinterpret_cast<const void *>(kernel);
+  std::lock_guard<std::mutex> guard(lock);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   int n = 0;
-  check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, ljx::kBlock, 0),
+  check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, block, 0),
         "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   n = std::max(1, std::min(n, 8));
   cache.emplace(key, n);
@@ -402,15 +408,9 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   const double cand = rc * (1.0 + kGroupMargin);
   const int span = std::min(p.nall, e->c.max_atoms);
   const int groups = (p.inum + ljx::kGroupRows - 1) / ljx::kGroupRows;
-  static int build_per_sm = 0;
-  if (build_per_sm == 0) {
-    check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&build_per_sm, ljx::k_build_groups<T>,
-                                                        ljx::kBuildBlock, 0),
-          "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    build_per_sm = std::max(1, build_per_sm);
-  }
   const int bgrid = std::max(1, std::min((groups + ljx::kBuildWarps - 1) / ljx::kBuildWarps,
-                                         e->sm_count * build_per_sm));
+                                         e->sm_count * blocks_per_sm(ljx::k_build_groups<T>,
+                                                                     ljx::kBuildBlock)));
   ljx::k_build_groups<T><<<bgrid, ljx::kBuildBlock, 0, s>>>(p, span, rebuild ? 1 : 0, disp_limit,
                                                             cand * cand);
   check_launch("k_build_groups");

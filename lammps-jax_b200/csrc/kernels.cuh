@@ -2,6 +2,8 @@
 // ("warp per row"): lanes take consecutive slots, a ballot compacts the kept pairs, per-row sums
 // finish with warp shuffles, and only scatters to a neighbor's row (half lists, newton-on ghost
 // rows) use atomics. Grids are persistent: a multiple of the SM count, warps stride over rows.
+// The row-group density pass over the candidate cache lives in groups.cuh; k_density here is the
+// list pass (cache off, and the compaction behind ljx_pack_edges).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -251,7 +253,8 @@ __device__ __forceinline__ bool pack_keep(const Step<T> &p, int i, const double4
 }
 
 // a1: LAMMPS x/type -> xd4 and its float copy (cpp/pair_jax_kokkos.cpp:35-52), plus the
-// largest |coordinate| (atomic max on float bits; *coord_bound is zeroed before the launch).
+// largest |coordinate| and, when a candidate cache exists, the largest squared displacement since
+// it was built (atomic max on float bits; both words are zeroed before the launch).
 template <typename T>
 __global__ void __launch_bounds__(kBlock) k_pack_atoms(const Step<T> p, int span)
 {
