@@ -37,6 +37,23 @@ METRIC = "EAM atom-steps/s (force+energy+virial)"
 UNIT = "atom-steps/s"
 CUTOFF, SKIN, A_CU, JITTER = 6.5, 2.0, 3.615, 0.08
 
+# Bench workloads. c3: weak scaling, 80^3 cells per GPU,
+# single-species Cu, full list, newton off. c4: strong scaling, 160^3 cells in all split into
+# z-slabs, binary Cu-Zr 64/36, half list with newton on (the half-unique communicating export).
+CONFIGS = {
+    "c3": {"cells": 80, "strong": False, "elements": ("Cu",), "fractions": None, "newton": False,
+           "half": False, "scaling": "weak", "lattice": A_CU,
+           "title": "C3: Cu fcc {c}^3 cells per GPU, synthetic EAM rc 6.5 A skin 2.0 A, full list, "
+                    "newton off, forward F'(rho) exchange"},
+    # C4 names no lattice constant; Vegard's law between the synthetic Cu (3.615 A) and Zr
+    # (4.525 A) lattices at 64/36 keeps the random alloy near zero pressure.
+    "c4": {"cells": 160, "strong": True, "elements": ("Cu", "Zr"), "fractions": (0.64, 0.36),
+           "newton": True, "half": True, "scaling": "strong", "lattice": 0.64 * 3.615 + 0.36 * 4.525,
+           "title": "C4: binary Cu-Zr (64/36) fcc {c}^3 cells in all (a = 3.943 A), split over the GPUs, "
+                    "synthetic EAM rc 6.5 A skin 2.0 A, half list, newton on, reverse rho + "
+                    "forward F'(rho) + reverse force exchanges"},
+}
+
 
 def package():
     name = "lammps_jax_b200"
@@ -146,40 +163,52 @@ def run_ljx(args):
         import datetime
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=datetime.timedelta(seconds=180))
-    cells = (args.cells, args.cells, args.cells)
     precision = args.precision
-    if world > 1:
-        system, nlocal, nall, decomp = setup_decomposed(ljx, cells, rank, world, precision, local)
+    cfg = CONFIGS[args.config]
+    if cfg["strong"]:
+        total = args.cells or cfg["cells"]
+        if total % world:
+            raise SystemExit(f"--config {args.config}: {total} z-cells do not split over {world} GPUs")
+        cells = (total, total, total // world)
     else:
-        system, nlocal, nall, decomp = setup_single(ljx, cells, precision)
+        n = args.cells or cfg["cells"]
+        cells = (n, n, n)
+    if world > 1:
+        system, nlocal, nall, decomp = setup_decomposed(ljx, cfg, cells, rank, world, precision,
+                                                        local)
+    else:
+        system, nlocal, nall, decomp = setup_single(ljx, cfg, cells, precision)
     pair = decomp["pair"]
+    plan = pair.plan
+    newton = system.newton_pair
     stream = torch.cuda.current_stream()
     eng = pair.engine
     atoms = system.atoms()
     nl = system.list.struct()
     fp_rows, width, elem = eng.feature_rows(1)
+    rho_rows = eng.feature_rows(0)[0]
 
     names = ["pack_atoms", "density", "embed", "halo_fp", "force", "result"]
     tick = [0]
 
-    def step(events=None):
-        def mark(k):
-            if events is not None:
-                events[k].record(stream)
-        # neighbor->ago as LAMMPS reports it with a rebuild every `rebuild_every` steps; the
-        # engine rebuilds its candidate cache on ago == 0 (-1: cache off).
-        nl.ago = tick[0] % args.rebuild_every if args.rebuild_every > 0 else -1
-        tick[0] += 1
+    def core(ago, mark=lambda k: None):
+        """One pair-style step on device data, with the exchanges the engine's plan asks for."""
+        nl.ago = ago
         mark(0)
         eng.pack_atoms(atoms)
         mark(1)
-        eng.density(atoms, nl, False)
+        eng.density(atoms, nl, newton)
+        if plan.reverse_density:
+            system.comm.reverse(rho_rows, width, elem)
         mark(2)
         eng.embed(atoms)
         mark(3)
-        system.comm.forward(fp_rows, width, elem)
+        if plan.forward_fp:
+            system.comm.forward(fp_rows, width, elem)
         mark(4)
-        eng.force(atoms, nl, False, 1.0)
+        eng.force(atoms, nl, newton, 1.0)
+        if plan.reverse_force:
+            system.comm.reverse_forces(system.f)  # LAMMPS's own reverse comm of ghost forces
         mark(5)
         res = eng.read_result()
         if world > 1:
@@ -190,6 +219,16 @@ def run_ljx(args):
                 raise RuntimeError("LAMMPS-JAX edge capacity exceeded")
         mark(6)
         return res
+
+    def step(events=None):
+        def mark(k):
+            if events is not None:
+                events[k].record(stream)
+        # neighbor->ago as LAMMPS reports it with a rebuild every `rebuild_every` steps; the
+        # engine rebuilds its candidate cache on ago == 0 (-1: cache off).
+        ago = tick[0] % args.rebuild_every if args.rebuild_every > 0 else -1
+        tick[0] += 1
+        return core(ago, mark)
 
     system.f.zero_()
     for _ in range(args.warmup):
@@ -238,19 +277,28 @@ def run_ljx(args):
     kname = {"density": (f"k_density_groups_full_{precision}" if cached
                          else f"k_density_full_{precision}"),
              "force": f"k_force_rows_full_{precision}"}[kernel]
-    traffic = profile_traffic(kname)
+    # The committed DRAM captures are of the C3 kernels (full list, newton off).
+    traffic = profile_traffic(kname) if args.config == "c3" else None
 
-    e2e = None if args.skip_extras else run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows,
-                                                 width, elem, args, nall, world, decomp["lists"])
-    value = world * nlocal * args.steps / elapsed
+    total_atoms, energy_total = nlocal, res.energy
+    if world > 1:
+        t = torch.tensor([nlocal], dtype=torch.int64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_atoms = int(t.item())
+        t = torch.tensor([res.energy], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        energy_total = float(t.item())
+    e2e = None if args.skip_extras else run_e2e(torch, system, core, args, world,
+                                                 decomp["lists"], total_atoms)
+    value = total_atoms * args.steps / elapsed
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None,
         "dtype": "f64" if precision == "float64" else "f32", "data": "synthetic",
         "config": {
-            "workload": f"C3: Cu fcc {args.cells}^3 cells ({nlocal:,} atoms) per GPU, synthetic "
-                        "EAM rc 6.5 A skin 2.0 A, full list, newton off, forward F'(rho) exchange",
+            "workload": cfg["title"].format(c=cells[0]) + f" ({total_atoms:,} atoms in all)",
+            "name": args.config, "total_atoms": total_atoms,
             "atoms_per_gpu": nlocal, "ghosts_per_gpu": nall - nlocal,
             "listed_pairs_per_atom": listed / nlocal, "kept_edges_per_atom": kept / nlocal,
             "precision": precision, "l2": "inputs larger than L2 (neighbor list "
@@ -273,9 +321,9 @@ def run_ljx(args):
                                     "per-launch algorithmic bytes"},
         "gpu_launches": launches,
         "e2e": e2e,
-        "energy_per_atom": res.energy / nlocal,
+        "energy_per_atom": energy_total / total_atoms,
     }
-    if world == 1 and not args.skip_extras:
+    if world == 1 and not args.skip_extras and args.config == "c3":
         line["cpu_baseline"] = cpu_baseline(args)
     clocks_summary = clocks.summary()
     line["clocks"] = clocks_summary
@@ -289,70 +337,86 @@ def run_ljx(args):
         dist.destroy_process_group()
 
 
-def setup_single(ljx, cells, precision):
+def _types_fn(cfg):
+    if cfg["fractions"] is None:
+        return None
+    ljx = package()
+    return lambda n, seed: ljx.synth.substitutional(n, cfg["fractions"], seed=seed)
+
+
+def _bundle(ljx, cfg, path, max_atoms, precision):
+    text = ljx.synth.synthetic_setfl(cfg["elements"])
+    # Edge capacity per atom: 128 for full lists (C3 keeps ~86 per row), 64 for half lists
+    # (~43 per row), which also keeps max_edges inside the contract's int range at 16.4 M atoms.
+    per_atom = 64 if cfg["half"] else 128
+    ljx.write_bundle(path, potential=ljx.eam_potential(text), max_atoms=max_atoms,
+                     max_edges=max_atoms * per_atom, cutoff=CUTOFF, unit_style="metal",
+                     precision=precision, force_output="atom-force",
+                     newton="on" if cfg["newton"] else "off", comm=True, half_edges=cfg["half"],
+                     n_species=len(cfg["elements"]))
+
+
+def setup_single(ljx, cfg, cells, precision):
     import tempfile
 
     import torch
-    atoms, x_all, owner, types_all = workload(cells)
+    types_fn = _types_fn(cfg)
+    n = 4 * cells[0] * cells[1] * cells[2]
+    types = types_fn(n, 2025) if types_fn else None
+    atoms = ljx.synth.fcc(cells, cfg["lattice"], jitter=JITTER, seed=2024, types=types)
+    x_all, owner = ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)
+    types_all = np.concatenate([atoms.types, atoms.types[owner]]).astype(np.int32)
     nlocal, nall = len(atoms.x), len(x_all)
-    text = ljx.synth.synthetic_setfl(("Cu",))
-    tmp = Path(tempfile.mkdtemp())
-    path = tmp / "c3.json"
-    max_atoms = nall + 1024
-    ljx.write_bundle(path, potential=ljx.eam_potential(text), max_atoms=max_atoms,
-                     max_edges=max_atoms * 128, cutoff=CUTOFF, unit_style="metal",
-                     precision=precision, force_output="atom-force", newton="off", comm=True,
-                     n_species=1)
+    path = Path(tempfile.mkdtemp()) / "bench.json"
+    _bundle(ljx, cfg, path, nall + 1024, precision)
     x = torch.as_tensor(x_all, device="cuda")
     system = ljx.System(x=x, type=torch.as_tensor(types_all, device="cuda"),
                         f=torch.zeros_like(x), nlocal=nlocal, nghost=nall - nlocal,
-                        newton_pair=False, unit_style="metal", ntypes=1)
+                        newton_pair=cfg["newton"], unit_style="metal",
+                        ntypes=len(cfg["elements"]))
     pair = ljx.PairJax()
     pair.coeff(system, "*", "*", str(path))
     pair.init_style(system)
-    builder = ljx.synth.DeviceListBuilder(x_all, nlocal, CUTOFF + SKIN, half=False)
+    builder = ljx.synth.DeviceListBuilder(x_all, nlocal, CUTOFF + SKIN, half=cfg["half"])
     system.list = builder.build(x)
     system.comm = ljx.SelfComm(torch.as_tensor(owner, device="cuda"), nlocal)
     return system, nlocal, nall, {"pair": pair, "parallelism": "single GPU (periodic self-images)",
                                   "comm_launches": 1, "lists": builder}
 
 
-def setup_decomposed(ljx, cells, rank, world, precision, local):
-    """Rank `rank` of a z-slab decomposition: 2,048,000 owned atoms per rank (weak scaling)."""
+def setup_decomposed(ljx, cfg, cells, rank, world, precision, local):
+    """Rank `rank` of a z-slab decomposition of `cells` per rank."""
     import tempfile
 
     import torch
     from importlib import import_module
     halo = import_module("lammps_jax_b200.halo")
-    slab = ljx.synth.slab_decomposition(cells, A_CU, JITTER, 2024, rank, world, CUTOFF + SKIN)
+    slab = ljx.synth.slab_decomposition(cells, cfg["lattice"], JITTER, 2024, rank, world,
+                                        CUTOFF + SKIN, types_fn=_types_fn(cfg))
     nlocal, nall = slab.nlocal, len(slab.x)
-    text = ljx.synth.synthetic_setfl(("Cu",))
-    tmp = Path(tempfile.mkdtemp())
-    path = tmp / f"c3_rank{rank}.json"
-    max_atoms = nall + 1024
-    ljx.write_bundle(path, potential=ljx.eam_potential(text), max_atoms=max_atoms,
-                     max_edges=max_atoms * 128, cutoff=CUTOFF, unit_style="metal",
-                     precision=precision, force_output="atom-force", newton="off", comm=True,
-                     n_species=1)
+    path = Path(tempfile.mkdtemp()) / f"bench_rank{rank}.json"
+    _bundle(ljx, cfg, path, nall + 1024, precision)
     x = torch.as_tensor(slab.x, device="cuda")
     system = ljx.System(x=x, type=torch.as_tensor(slab.types, device="cuda"),
                         f=torch.zeros_like(x), nlocal=nlocal, nghost=nall - nlocal,
-                        newton_pair=False, unit_style="metal", ntypes=1)
+                        newton_pair=cfg["newton"], unit_style="metal",
+                        ntypes=len(cfg["elements"]))
     pair = ljx.PairJax(device=local)
     pair.coeff(system, "*", "*", str(path))
     pair.init_style(system)
-    builder = ljx.synth.DeviceListBuilder(slab.x, nlocal, CUTOFF + SKIN, half=False)
+    builder = ljx.synth.DeviceListBuilder(slab.x, nlocal, CUTOFF + SKIN, half=cfg["half"])
     system.list = builder.build(x)
     elem = 8 if precision == "float64" else 4
     system.comm = halo.SlabExchange(slab, 1, elem)
+    exchanges = "reverse rho, forward F'(rho) and reverse forces" if cfg["newton"] else "F'(rho)"
     return system, nlocal, nall, {
         "pair": pair, "comm_launches": system.comm.launches_per_exchange, "lists": builder,
-        "parallelism": f"z-slab spatial decomposition over {world} GPUs, F'(rho) halo by "
-                       "grouped NCCL send/recv with both z-neighbors + x/y periodic images",
+        "parallelism": f"z-slab spatial decomposition over {world} GPUs; {exchanges} by grouped "
+                       "NCCL send/recv with both z-neighbors + x/y periodic images",
         "close": lambda: None}
 
 
-def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall, world, lists):
+def run_e2e(torch, system, core, args, world, lists, total_atoms):
     """Same step through the C ABI with host buffers: H2D of x and D2H of the forces and the
     result every step. Every 10th step (the C3 rebuild period) the neighbor list is rebuilt on
     the device from the uploaded positions (ljx_neigh_bin + ljx_neigh_build into the same
@@ -366,14 +430,9 @@ def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall
         system.x.copy_(x_host, non_blocking=True)
         if k % 10 == 0:
             lists.launch(system.x, stream)
-        nl.ago = k % 10 if args.rebuild_every > 0 else -1
-        eng.pack_atoms(atoms)
-        eng.density(atoms, nl, False)
-        eng.embed(atoms)
-        system.comm.forward(fp_rows, width, elem)
-        eng.force(atoms, nl, False, 1.0)
+        core(k % 10 if args.rebuild_every > 0 else -1)  # ends with the result read (a sync)
         f_host.copy_(system.f, non_blocking=True)
-        eng.read_result()  # synchronizes the stream: forces and energy are on the host
+        torch.cuda.current_stream().synchronize()        # forces on the host
         return x_host.numel() * 8
 
     one(1)
@@ -386,7 +445,12 @@ def run_e2e(ljx, torch, system, eng, atoms, nl, fp_rows, width, elem, args, nall
     stop.record(stream)
     torch.cuda.synchronize()
     elapsed = start.elapsed_time(stop) / 1e3
-    value = world * system.nlocal * steps / elapsed
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([elapsed], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    value = total_atoms * steps / elapsed
     return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d / steps,
             "d2h_bytes_per_step": f_host.numel() * 8 + 9 * 8, "steps": steps,
             "list": "rebuilt on the device every 10th step from the uploaded positions"}
@@ -471,8 +535,12 @@ def main():
     ap.add_argument("--rebuild-every", type=int, default=10,
                     help="neighbor rebuild period the engine is told (neighbor->ago); C3 "
                          "rebuilds every 10 steps. 0 turns the candidate cache off")
-    ap.add_argument("--cells", type=int, default=80,
-                    help="fcc cells per edge of each rank's box (80 = the 2,048,000-atom config)")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c3",
+                    help="c3: weak scaling (the default bench line); c4: strong scaling of the "
+                         "16.4 M-atom binary crystal")
+    ap.add_argument("--cells", type=int, default=None,
+                    help="fcc cells per edge: of each rank's box for c3 (default 80, the "
+                         "2,048,000-atom config), of the whole box for c4 (default 160)")
     ap.add_argument("--skip-extras", action="store_true",
                     help="time the device path only (no e2e or CPU-baseline legs); for profiling")
     args = ap.parse_args()

@@ -5,7 +5,8 @@
    ranks, reproduces the all-pairs minimum-image forces and energy of the whole periodic crystal
    (the oracle runs the ranks as one combined system whose ghost rows point at owners on any rank).
 3. Transport: SlabExchange over a real 2-rank gloo process group fills every ghost row with its
-   owner's value (host pack/unpack stand-ins; on GPUs the ljx_comm_* kernels do this).
+   owner's value (forward) and adds every ghost row back into its owner (reverse), with host
+   stand-ins for the row operations (on GPUs the ljx_comm_* kernels do them).
 """
 
 import os
@@ -109,6 +110,34 @@ def test_decomposed_physics_matches_whole_crystal(ljx, oracle):
     assert np.max(np.abs(out.virial - v_ref)) <= 1e-11 * np.max(np.abs(v_ref))
 
 
+class HostRowOps:
+    """The row operations of halo.GpuRowOps on CPU tensors (width-1 double rows), so the
+    transport runs over a real gloo process group without a GPU."""
+
+    def pack_forward(self, rows, w, e, sendlist, buf):
+        buf[: sendlist.numel()] = rows[sendlist.long()]
+
+    def unpack_forward(self, rows, w, e, first, n, buf):
+        rows[first:first + n] = buf[:n]
+
+    def self_forward(self, rows, w, e, owner, first):
+        rows[first:first + owner.numel()] = rows[owner.long()]
+
+    def self_reverse(self, rows, w, e, owner, first):
+        n = owner.numel()
+        rows.index_add_(0, owner.long(), rows[first:first + n].clone())
+        rows[first:first + n] = 0
+
+    def pack_reverse(self, rows, w, e, first, n, buf):
+        buf[:n] = rows[first:first + n]
+
+    def unpack_reverse(self, rows, w, e, sendlist, buf):
+        rows.index_add_(0, sendlist.long(), buf[: sendlist.numel()].clone())
+
+    def zero_rows(self, rows, w, e, first, n):
+        rows[first:first + n] = 0
+
+
 def _exchange_worker(rank, nranks, port, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=nranks)
@@ -118,22 +147,22 @@ def _exchange_worker(rank, nranks, port, results):
         parts = slabs(ljx, nranks)
         s = parts[rank]
         owners, offsets = combined_owner(parts)
+        ex = SlabExchange(s, 1, 8, device="cpu", ops=HostRowOps())
+        # Forward: every ghost row takes its owner's value (the owner's combined index).
         rows = torch.full((len(s.x),), -1.0, dtype=torch.float64)
         rows[:s.nlocal] = torch.arange(s.nlocal, dtype=torch.float64) + float(offsets[rank])
-
-        def pack(rows_t, sendlist, buf):
-            buf[: sendlist.numel()] = rows_t[sendlist.long()]
-
-        def unpack(rows_t, first, n, buf):
-            rows_t[first:first + n] = buf[:n]
-
-        def self_fill(rows_t):
-            first = s.nlocal + s.n_low + s.n_up
-            rows_t[first:] = rows_t[torch.as_tensor(s.xy_owner).long()]
-
-        ex = SlabExchange(s, 1, 8, device="cpu", pack=pack, unpack=unpack, self_fill=self_fill)
         ex.forward(rows)
-        results[rank] = bool(np.array_equal(rows[s.nlocal:].numpy(), owners[rank].astype(float)))
+        forward_ok = bool(np.array_equal(rows[s.nlocal:].numpy(), owners[rank].astype(float)))
+        # Reverse: every ghost row carries 1; each owned row must end up with the number of its
+        # ghost copies on all ranks, and every ghost row with 0.
+        rows = torch.zeros(len(s.x), dtype=torch.float64)
+        rows[s.nlocal:] = 1.0
+        ex.reverse(rows)
+        counts = np.bincount(np.concatenate(owners), minlength=int(offsets[-1]))
+        mine = counts[offsets[rank]:offsets[rank] + s.nlocal].astype(float)
+        reverse_ok = bool(np.array_equal(rows[:s.nlocal].numpy(), mine) and
+                          not np.any(rows[s.nlocal:].numpy()))
+        results[rank] = (forward_ok, reverse_ok)
     finally:
         dist.destroy_process_group()
 
@@ -149,4 +178,4 @@ def test_slab_exchange_over_gloo(nranks):
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.spawn(_exchange_worker, args=(nranks, free_port(), results), nprocs=nranks, join=True)
-    assert dict(results) == {r: True for r in range(nranks)}
+    assert dict(results) == {r: (True, True) for r in range(nranks)}
