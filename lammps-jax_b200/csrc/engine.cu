@@ -108,6 +108,9 @@ struct ljx_engine {
   bool groups_valid = false;
   GroupKey groups_key{};
   long long group_builds = 0;  // host-requested cache builds
+  int list_age_steps = 0;      // density calls since the last fresh list (ago == 0)
+  int list_period = 1 << 30;   // lifetime in steps of the previous list (unknown at first)
+  bool period_cached = true;   // the current list's steps run over the candidate cache
   int *senders = nullptr;
   int *receivers = nullptr;
   uint8_t *edge_mask = nullptr;
@@ -392,6 +395,8 @@ void launch_density(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
 // Cache margin as a fraction of the pack cutoff: unions hold pairs within rc (1 + margin) and
 // stay valid until some atom has moved rc * margin / 2.
 constexpr double kGroupMargin = 0.08;
+// Shortest list lifetime (steps) for which the candidate cache is built.
+constexpr int kCacheMinPeriod = 4;
 
 template <typename T>
 void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago, int mode)
@@ -530,11 +535,24 @@ ljx_status density_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const
     const long long rows = std::min<long long>(p.nall, e->c.max_atoms);
     check(cudaMemsetAsync(e->rho, 0, rows * sizeof(T), s), "cudaMemsetAsync(rho)");
   }
-  if (l->ago < 0 || e->xref == nullptr) {
-    launch_density<T>(e, s, p, m.density);
-  } else {
-    launch_groups<T>(e, s, p, l->ago, m.density);
+  // Candidate cache policy. A build costs about as much as one list pass plus a third, and each
+  // later step over the cache saves about a quarter of a list pass (C3), so a list has to live
+  // kCacheMinPeriod steps for the cache to pay. LAMMPS rebuilds lists at a steady rhythm, so
+  // the previous list's lifetime decides, at each fresh list, whether its steps use the cache.
+  bool cached = l->ago >= 0 && e->xref != nullptr;
+  if (cached) {
+    if (l->ago == 0) {
+      if (e->list_age_steps > 0) e->list_period = e->list_age_steps;
+      e->list_age_steps = 0;
+      e->period_cached = e->list_period >= kCacheMinPeriod;
+    }
+    ++e->list_age_steps;
+    cached = e->period_cached;
   }
+  if (cached)
+    launch_groups<T>(e, s, p, l->ago, m.density);
+  else
+    launch_density<T>(e, s, p, m.density);
   e->last_duplicate = m.duplicate ? 2 : 1;
   return LJX_OK;
 }

@@ -104,3 +104,21 @@ def test_cache_off_walks_the_list(tmp_path, oracle, mode):
         system.comm.reverse_forces(system.f)
     torch.cuda.synchronize()
     assert_parity(res, system, oracle_step(oracle, case, system, mode, "float64"), "float64", case)
+
+
+def test_cache_policy_over_list_ages(tmp_path, oracle):
+    """The engine caches candidates for a fresh list only if the previous list lived at least 4
+    steps; otherwise that list's steps take the list pass. A sequence with long lists, a list of
+    one step and the switch back covers cached, rebuilt and list-pass steps; every step matches
+    the oracle."""
+    case = eam_case(elements=("Cu", "Zr"), cells=(5, 5, 5), seed=43, nr=2000, nrho=2000)
+    pair, system, res = run_pair(tmp_path, case, "rows-full", "float64")
+    rng = np.random.default_rng(9)
+    limit = 0.5 * MARGIN * case.cutoff
+    for ago in (1, 2, 3, 4, 0, 1, 2, 3, 4, 0, 0, 1, 2, 3, 4, 0, 1):
+        d = rng.normal(size=(case.nlocal, 3))
+        d *= (0.2 * limit * rng.random((case.nlocal, 1))) / np.linalg.norm(d, axis=1, keepdims=True)
+        case = moved_case(case, d)
+        res = step_again(pair, system, case, ago)
+        ref = oracle_step(oracle, case, system, "rows-full", "float64")
+        assert_parity(res, system, ref, "float64", case)
