@@ -17,6 +17,11 @@ with "impl": "reference".
 Multi-GPU runs (torchrun, one rank per GPU) use spatial decomposition along z: every rank owns a
 2,048,000-atom slab of a larger crystal (weak scaling) and exchanges F'(rho) of its boundary
 atoms with its two z-neighbors over NCCL each step.
+
+--config c4 is the strong-scaling case (16,384,000-atom binary crystal split over the GPUs, half
+list, newton on: reverse rho, forward F'(rho) and reverse force exchanges). --config c5 is the
+edge-pack stress test on one GPU (2,048,000-atom dense binary liquid, float32, fresh list every
+step, about half the listed pairs outside rc).
 """
 
 from __future__ import annotations
@@ -37,21 +42,34 @@ METRIC = "EAM atom-steps/s (force+energy+virial)"
 UNIT = "atom-steps/s"
 CUTOFF, SKIN, A_CU, JITTER = 6.5, 2.0, 3.615, 0.08
 
-# Bench workloads. c3: weak scaling, 80^3 cells per GPU,
+# Bench workloads ([3] and [4]). c3: weak scaling, 80^3 cells per GPU,
 # single-species Cu, full list, newton off. c4: strong scaling, 160^3 cells in all split into
 # z-slabs, binary Cu-Zr 64/36, half list with newton on (the half-unique communicating export).
+# c5: the edge-pack stress test, a dense binary liquid in float32 with a fresh list every step.
 CONFIGS = {
     "c3": {"cells": 80, "strong": False, "elements": ("Cu",), "fractions": None, "newton": False,
-           "half": False, "scaling": "weak", "lattice": A_CU,
+           "half": False, "scaling": "weak", "lattice": A_CU, "edges_per_atom": 128,
            "title": "C3: Cu fcc {c}^3 cells per GPU, synthetic EAM rc 6.5 A skin 2.0 A, full list, "
                     "newton off, forward F'(rho) exchange"},
     # C4 names no lattice constant; Vegard's law between the synthetic Cu (3.615 A) and Zr
     # (4.525 A) lattices at 64/36 keeps the random alloy near zero pressure.
+    # Edge capacity 64 per atom for the half list (~43 kept per row) also keeps max_edges inside
+    # the contract's int range at 16.4 M atoms.
     "c4": {"cells": 160, "strong": True, "elements": ("Cu", "Zr"), "fractions": (0.64, 0.36),
            "newton": True, "half": True, "scaling": "strong", "lattice": 0.64 * 3.615 + 0.36 * 4.525,
+           "edges_per_atom": 64,
            "title": "C4: binary Cu-Zr (64/36) fcc {c}^3 cells in all (a = 3.943 A), split over the GPUs, "
                     "synthetic EAM rc 6.5 A skin 2.0 A, half list, newton on, reverse rho + "
                     "forward F'(rho) + reverse force exchanges"},
+    # 1.2x the synthetic Cu fcc density (0.1016 atoms/A^3) with a 2.0 A hard core: a liquid tile
+    # of 32,000 atoms (synth.liquid_packing) repeated (cells/20)^3 times, 4 * cells^3 atoms in
+    # all. With the 2.0 A skin about half the listed pairs fall outside rc.
+    "c5": {"cells": 80, "strong": False, "elements": ("Cu", "Zr"), "fractions": (0.64, 0.36),
+           "newton": False, "half": False, "scaling": "weak", "liquid": 1.2 * 4 / A_CU ** 3,
+           "edges_per_atom": 160, "precision": "float32", "rebuild_every": 1, "one_gpu": True,
+           "title": "C5: edge-pack stress test, binary Cu-Zr (64/36) liquid at 1.2x fcc density "
+                    "with a 2.0 A core, {c}^3-cell equivalent, synthetic EAM rc 6.5 A skin 2.0 A, "
+                    "full list, newton off, fresh list every step"},
 }
 
 
@@ -92,17 +110,38 @@ class ClockSampler:
         self.proc = None
         self.index = index
 
+    def _gpu_id(self):
+        """nvidia-smi's name for torch device `index`: its UUID (CUDA_VISIBLE_DEVICES renumbers
+        the devices torch sees, nvidia-smi does not)."""
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            return str(self.index)
+
     def __enter__(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
+            self.path.parent.mkdir(parents=True, exist_ok=True)
             self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self._gpu_id()}",
+                                          f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a few hundred ms to print its first sample; a timed region of a few
+        # hundred ms would otherwise end before it. Wait (at most 5 s) for that sample.
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.fh.flush()
+            if self.path.stat().st_size > 0:
+                break
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):
@@ -163,8 +202,12 @@ def run_ljx(args):
         import datetime
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=datetime.timedelta(seconds=180))
-    precision = args.precision
     cfg = CONFIGS[args.config]
+    precision = args.precision or cfg.get("precision", "float64")
+    if args.rebuild_every is None:
+        args.rebuild_every = cfg.get("rebuild_every", 10)
+    if cfg.get("one_gpu") and world > 1:
+        raise SystemExit(f"--config {args.config} runs on one GPU")
     if cfg["strong"]:
         total = args.cells or cfg["cells"]
         if total % world:
@@ -231,18 +274,16 @@ def run_ljx(args):
         return core(ago, mark)
 
     system.f.zero_()
-    for _ in range(args.warmup):
-        res = step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    launches0 = eng.launches
     kevents = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The clock samples span the warm-up and the timed steps (both under load).
     with ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv") as clocks:
+        for _ in range(args.warmup):
+            res = step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
+        launches0 = eng.launches
         start.record(stream)
         for k in range(args.steps):
             res = step(kevents[k])
@@ -273,7 +314,9 @@ def run_ljx(args):
     kbytes = bytes_density if kernel == "density" else bytes_force
     achieved = kbytes / phase[kernel] / 1e9
     peak, peak_kind = peaks()
-    cached = args.rebuild_every > 0
+    # The engine caches candidates only for lists that live at least 4 steps (kCacheMinPeriod in
+    # csrc/engine.cu); shorter-lived lists take the list pass.
+    cached = args.rebuild_every >= 4
     kname = {"density": (f"k_density_groups_full_{precision}" if cached
                          else f"k_density_full_{precision}"),
              "force": f"k_force_rows_full_{precision}"}[kernel]
@@ -288,6 +331,7 @@ def run_ljx(args):
         t = torch.tensor([res.energy], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         energy_total = float(t.item())
+    neigh_ms = time_list_build(torch, decomp["lists"], system.x, stream)
     e2e = None if args.skip_extras else run_e2e(torch, system, core, args, world,
                                                  decomp["lists"], total_atoms)
     value = total_atoms * args.steps / elapsed
@@ -303,11 +347,17 @@ def run_ljx(args):
             "listed_pairs_per_atom": listed / nlocal, "kept_edges_per_atom": kept / nlocal,
             "precision": precision, "l2": "inputs larger than L2 (neighbor list "
                                            f"{system.list.neighbors.numel() * 4 / 1e9:.2f} GB)",
-            "list": "built once on the device, fixed over timed steps",
+            "list": ("built once on the device, fixed over timed steps; the engine is told "
+                     "neighbor->ago = 0 every step, so every step compacts the whole list as "
+                     "after a rebuild; the device rebuild itself is timed apart (neigh_build_ms)"
+                     if args.rebuild_every == 1 else
+                     "built once on the device, fixed over timed steps"),
+            "neigh_build_ms": neigh_ms,
             "rebuild_every": args.rebuild_every,
             "candidate_cache": ("rebuilt when neighbor->ago == 0, every "
                                 f"{args.rebuild_every} steps, inside the timed region"
-                                if args.rebuild_every > 0 else "off (every step filters the list)"),
+                                if cached else "not used: every step filters the whole list "
+                                "(lists living under 4 steps, or the cache turned off)"),
             "parallelism": decomp["parallelism"],
             "phase_ms": {n: v * 1e3 for n, v in phase.items()},
         },
@@ -324,6 +374,7 @@ def run_ljx(args):
         "energy_per_atom": energy_total / total_atoms,
     }
     if world == 1 and not args.skip_extras and args.config == "c3":
+        line["md"] = run_md(torch, ljx, cfg, cells, precision, args.steps, args.warmup)
         line["cpu_baseline"] = cpu_baseline(args)
     clocks_summary = clocks.summary()
     line["clocks"] = clocks_summary
@@ -346,9 +397,7 @@ def _types_fn(cfg):
 
 def _bundle(ljx, cfg, path, max_atoms, precision):
     text = ljx.synth.synthetic_setfl(cfg["elements"])
-    # Edge capacity per atom: 128 for full lists (C3 keeps ~86 per row), 64 for half lists
-    # (~43 per row), which also keeps max_edges inside the contract's int range at 16.4 M atoms.
-    per_atom = 64 if cfg["half"] else 128
+    per_atom = cfg["edges_per_atom"]
     ljx.write_bundle(path, potential=ljx.eam_potential(text), max_atoms=max_atoms,
                      max_edges=max_atoms * per_atom, cutoff=CUTOFF, unit_style="metal",
                      precision=precision, force_output="atom-force",
@@ -356,14 +405,27 @@ def _bundle(ljx, cfg, path, max_atoms, precision):
                      n_species=len(cfg["elements"]))
 
 
+def liquid_atoms(ljx, cfg, cells):
+    """C5 positions: a 20^3-cell-equivalent liquid tile repeated (cells/20)^3 times (one tile of
+    4 * cells^3 atoms when cells is not a multiple of 20)."""
+    tiles, edge = (cells // 20, 20) if cells % 20 == 0 else (1, cells)
+    n_tile = 4 * edge ** 3
+    types = _types_fn(cfg)(n_tile, 2025)
+    return ljx.synth.liquid_packing(n_tile, cfg["liquid"], 2.0, seed=2024, tiles=tiles,
+                                    types=types)
+
+
 def setup_single(ljx, cfg, cells, precision):
     import tempfile
 
     import torch
     types_fn = _types_fn(cfg)
-    n = 4 * cells[0] * cells[1] * cells[2]
-    types = types_fn(n, 2025) if types_fn else None
-    atoms = ljx.synth.fcc(cells, cfg["lattice"], jitter=JITTER, seed=2024, types=types)
+    if cfg.get("liquid"):
+        atoms = liquid_atoms(ljx, cfg, cells[0])
+    else:
+        n = 4 * cells[0] * cells[1] * cells[2]
+        types = types_fn(n, 2025) if types_fn else None
+        atoms = ljx.synth.fcc(cells, cfg["lattice"], jitter=JITTER, seed=2024, types=types)
     x_all, owner = ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)
     types_all = np.concatenate([atoms.types, atoms.types[owner]]).astype(np.int32)
     nlocal, nall = len(atoms.x), len(x_all)
@@ -416,11 +478,70 @@ def setup_decomposed(ljx, cfg, cells, rank, world, precision, local):
         "close": lambda: None}
 
 
+def run_md(torch, ljx, cfg, cells, precision, steps, warmup):
+    """C3's own run: NVE at dt = 1 fs with a neighbor rebuild every 10 steps, through the pair
+    style (ljx_pair_compute) with the device MD step around it (lammps-jax_b200/md.py: fix nve
+    integration, forward comm of positions to the periodic images, the device list rebuild every
+    10th step). Seeded Gaussian velocities at 300 K. Times `steps` full MD steps after `warmup`."""
+    import tempfile
+    from importlib import import_module
+    md = import_module("lammps_jax_b200.md")
+    atoms = ljx.synth.fcc(cells, cfg["lattice"], jitter=JITTER, seed=2024)
+    n = len(atoms.x)
+    mass = np.array([ljx.synth.ELEMENTS[e]["mass"] for e in cfg["elements"]])
+    v0 = md.maxwell_velocities(mass[atoms.types - 1], 300.0, "metal", seed=2026)
+    nall = len(ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)[0])
+    path = Path(tempfile.mkdtemp()) / "md.json"
+    _bundle(ljx, cfg, path, int(1.05 * nall) + 1024, precision)
+    pair = ljx.PairJax()
+    run = md.NVE(pair, atoms.x, atoms.types, atoms.box, mass, cutoff=CUTOFF, skin=SKIN, dt=0.001,
+                 units="metal", newton_pair=cfg["newton"], half_list=cfg["half"], v=v0,
+                 every=10, check=False, borders="when-needed")
+    pair.coeff(run.system, "*", "*", str(path))
+    pair.init_style(run.system)
+    t0 = run.thermo(run.setup())
+    for _ in range(warmup):
+        run.step()
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(steps):
+        res = run.step(eflag=(k == steps - 1))
+    stop.record(stream)
+    torch.cuda.synchronize()
+    elapsed = start.elapsed_time(stop) / 1e3
+    t1 = run.thermo(res)
+    return {"value": n * steps / elapsed, "unit": UNIT, "ms_per_step": elapsed / steps * 1e3,
+            "steps": steps, "warmup": warmup, "dt_fs": 1.0, "rebuild_every": 10,
+            "list_builds": run.builds, "border_builds": run.border_builds,
+            "temp_start_K": t0.temp, "temp_end_K": t1.temp,
+            "etotal_drift_ev_per_atom": (t1.etotal - t0.etotal) / n,
+            "what": "full MD step on the device: fix nve initial/final integrate, forward comm "
+                    "of positions to the periodic images (the device list rebuild every 10th "
+                    "step), pair style compute through ljx_pair_compute (energy at the last "
+                    "step); velocities at 300 K"}
+
+
+def time_list_build(torch, lists, x, stream, reps=5):
+    """Device neighbor-list rebuild (ljx_neigh_bin + ljx_neigh_build) in ms, the mean of `reps`
+    rebuilds into the same buffers after one untimed."""
+    lists.launch(x, stream)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(reps):
+        lists.launch(x, stream)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / reps
+
+
 def run_e2e(torch, system, core, args, world, lists, total_atoms):
     """Same step through the C ABI with host buffers: H2D of x and D2H of the forces and the
-    result every step. Every 10th step (the C3 rebuild period) the neighbor list is rebuilt on
-    the device from the uploaded positions (ljx_neigh_bin + ljx_neigh_build into the same
-    buffers), as LAMMPS-Kokkos builds it on the device."""
+    result every step. Every `rebuild_every`-th step (10 for C3 and C4, every step for C5) the
+    neighbor list is rebuilt on the device from the uploaded positions (ljx_neigh_bin +
+    ljx_neigh_build into the same buffers), as LAMMPS-Kokkos builds it on the device."""
+    period = args.rebuild_every if args.rebuild_every > 0 else 10
     x_host = system.x.cpu().pin_memory()
     f_host = torch.empty_like(system.f, device="cpu").pin_memory()
     stream = torch.cuda.current_stream()
@@ -428,9 +549,9 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms):
 
     def one(k):
         system.x.copy_(x_host, non_blocking=True)
-        if k % 10 == 0:
+        if k % period == 0:
             lists.launch(system.x, stream)
-        core(k % 10 if args.rebuild_every > 0 else -1)  # ends with the result read (a sync)
+        core(k % period if args.rebuild_every > 0 else -1)  # ends with the result read (a sync)
         f_host.copy_(system.f, non_blocking=True)
         torch.cuda.current_stream().synchronize()        # forces on the host
         return x_host.numel() * 8
@@ -453,7 +574,9 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms):
     value = total_atoms * steps / elapsed
     return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d / steps,
             "d2h_bytes_per_step": f_host.numel() * 8 + 9 * 8, "steps": steps,
-            "list": "rebuilt on the device every 10th step from the uploaded positions"}
+            "list": ("rebuilt on the device every step from the uploaded positions" if period == 1
+                     else f"rebuilt on the device every {period}th step from the uploaded "
+                          "positions")}
 
 
 def cpu_baseline(args, sample_cells=(40, 40, 40), steps=None):
@@ -531,16 +654,19 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ljx", "reference"), default="ljx")
-    ap.add_argument("--precision", choices=("float64", "float32"), default="float64")
-    ap.add_argument("--rebuild-every", type=int, default=10,
-                    help="neighbor rebuild period the engine is told (neighbor->ago); C3 "
-                         "rebuilds every 10 steps. 0 turns the candidate cache off")
+    ap.add_argument("--precision", choices=("float64", "float32"), default=None,
+                    help="default: float64 (c3, c4), float32 (c5)")
+    ap.add_argument("--rebuild-every", type=int, default=None,
+                    help="neighbor rebuild period the engine is told (neighbor->ago); C3 and C4 "
+                         "rebuild every 10 steps (the default), C5 every step. 0 turns the "
+                         "candidate cache off")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c3",
                     help="c3: weak scaling (the default bench line); c4: strong scaling of the "
-                         "16.4 M-atom binary crystal")
+                         "16.4 M-atom binary crystal; c5: the edge-pack stress test (one GPU)")
     ap.add_argument("--cells", type=int, default=None,
                     help="fcc cells per edge: of each rank's box for c3 (default 80, the "
-                         "2,048,000-atom config), of the whole box for c4 (default 160)")
+                         "2,048,000-atom config), of the whole box for c4 (default 160); the "
+                         "fcc-cell equivalent of the liquid box for c5 (default 80)")
     ap.add_argument("--skip-extras", action="store_true",
                     help="time the device path only (no e2e or CPU-baseline legs); for profiling")
     args = ap.parse_args()

@@ -132,6 +132,12 @@ SIGNATURES = [
     ("ljx_neigh_build", c_int, [c_void_p, c_void_p, c_int, c_int, c_double, c_int, c_void_p,
                                 c_double, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong,
                                 c_int, c_void_p, c_void_p]),
+    ("ljx_nve_initial", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                c_double, POINTER(c_double), c_int]),
+    ("ljx_nve_final", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, POINTER(c_double),
+                              c_int]),
+    ("ljx_ghost_positions", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    ("ljx_max_displacement", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
 ]
 
 _lib: ctypes.CDLL | None = None

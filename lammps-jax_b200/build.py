@@ -3,7 +3,7 @@
     python -c "import importlib.util as u, sys; ..."   # or __graft_entry__.build()
 
 The library holds every kernel (csrc/*.cu) and the bundle loader (csrc/bundle.cpp) behind the
-C ABI of include/ljx.h and include/ljx_neigh.h.
+C ABI of include/ljx.h, include/ljx_neigh.h, include/ljx_pair.h and include/ljx_md.h.
 """
 
 from __future__ import annotations

@@ -37,6 +37,28 @@ def test_substitutional_counts(ljx):
     assert (t == 1).sum() == 640 and (t == 2).sum() == 360
 
 
+def test_liquid_packing(ljx):
+    """The C5 generator: density, the 2.0 A hard core across the periodic boundary, seeded, and
+    exact periodic tiles (every copy of a tile atom sits at the same place in its tile)."""
+    from scipy.spatial import cKDTree
+    density = 1.2 * 4 / 3.615 ** 3
+    types = ljx.synth.substitutional(4000, (0.64, 0.36), seed=1)
+    one = ljx.synth.liquid_packing(4000, density, 2.0, seed=7, types=types)
+    assert one.x.shape == (4000, 3) and np.all(one.x >= 0) and np.all(one.x < one.box)
+    assert len(one.x) / np.prod(one.box) == pytest.approx(density, rel=1e-12)
+    d, _ = cKDTree(one.x, boxsize=one.box).query(one.x, k=2)
+    assert d[:, 1].min() >= 2.0
+    again = ljx.synth.liquid_packing(4000, density, 2.0, seed=7, types=types)
+    np.testing.assert_array_equal(one.x, again.x)
+    tiled = ljx.synth.liquid_packing(4000, density, 2.0, seed=7, types=types, tiles=2)
+    assert len(tiled.x) == 32000 and np.allclose(tiled.box, 2 * one.box)
+    d, _ = cKDTree(tiled.x, boxsize=tiled.box).query(tiled.x, k=2)
+    assert d[:, 1].min() >= 2.0
+    key = lambda x, t: sorted(zip(map(tuple, np.round(np.mod(x, one.box), 6)), t))  # noqa: E731
+    assert key(tiled.x, tiled.types) == sorted(key(one.x, one.types) * 8)
+    assert np.bincount(tiled.types)[1:].tolist() == [8 * 2560, 8 * 1440]
+
+
 def test_binning_covers_all_atoms(ljx):
     rng = np.random.default_rng(0)
     x = rng.random((500, 3)) * 20.0
@@ -93,3 +115,15 @@ def test_plan_selects_list_kind(ljx, kw, newton, half):
     rule = (c["half_edges"] == 1) if (newton and comm) else (
         False if not newton else (c["force_layout"] == 1 or c["pair_sum"] == 1))
     assert rule == half
+
+
+@pytest.mark.parametrize("units,temp", [("lj", 0.7), ("metal", 600.0)])
+def test_maxwell_velocities(ljx, units, temp):
+    """velocity create ... dist gaussian mom yes: zero momentum, exactly T over 3N - 3 dof."""
+    masses = np.where(np.arange(500) % 3 == 0, 91.224, 63.546)
+    v = ljx.md.maxwell_velocities(masses, temp, units, seed=4)
+    u = ljx.md.UNITS[units]
+    assert np.allclose((masses[:, None] * v).sum(0), 0.0, atol=1e-10 * np.abs(v).max() * 500)
+    t = (masses[:, None] * v * v).sum() * u["mvv2e"] / ((3 * 500 - 3) * u["boltz"])
+    assert t == pytest.approx(temp, rel=1e-12)
+    np.testing.assert_array_equal(v, ljx.md.maxwell_velocities(masses, temp, units, seed=4))
