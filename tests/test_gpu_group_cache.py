@@ -122,3 +122,55 @@ def test_cache_policy_over_list_ages(tmp_path, oracle):
         res = step_again(pair, system, case, ago)
         ref = oracle_step(oracle, case, system, "rows-full", "float64")
         assert_parity(res, system, ref, "float64", case)
+
+
+def test_spilled_groups_walk_their_lists(tmp_path, oracle):
+    """A compacted row capacity of 40 gives every group a union capacity of 160 and a row
+    candidate capacity of 80, which C3-density rows (about 108 candidates) exceed: every group is
+    past capacity, and the cached steps walk the rows' lists instead."""
+    case = eam_case(cells=(5, 5, 5), seed=47, nr=2000, nrho=2000)
+    nall = len(case.x_all)
+    pair, system, res = run_pair(tmp_path, case, "rows-full", "float64",
+                                 max_atoms=nall + 64, max_edges=(nall + 64) * 40)
+    assert_parity(res, system, oracle_step(oracle, case, system, "rows-full", "float64"),
+                  "float64", case)
+    rng = np.random.default_rng(3)
+    limit = 0.5 * MARGIN * case.cutoff
+    for ago in (1, 2):
+        d = rng.normal(size=(case.nlocal, 3))
+        d *= (0.5 * limit * rng.random((case.nlocal, 1))) / np.linalg.norm(d, axis=1, keepdims=True)
+        case = moved_case(case, d)
+        res = step_again(pair, system, case, ago)
+        assert_parity(res, system, oracle_step(oracle, case, system, "rows-full", "float64"),
+                      "float64", case)
+
+
+def test_cache_build_is_deterministic(tmp_path):
+    """The cache build numbers each union in first-seen order of one warp's walk over the
+    group's lists, so a repeated run gives bitwise the same forces and energy on the build step
+    and on the cached steps after it. (Full list, newton off: every sum has a fixed order; the
+    newton-on modes scatter to neighbors with atomics.)"""
+    mode = "rows-full"
+    case = eam_case(elements=("Cu", "Zr"), cells=(5, 5, 5), seed=53, nr=2000, nrho=2000)
+    rng = np.random.default_rng(8)
+    limit = 0.5 * MARGIN * case.cutoff
+    moves = []
+    for _ in range(3):
+        d = rng.normal(size=(case.nlocal, 3))
+        d *= (0.5 * limit * rng.random((case.nlocal, 1))) / np.linalg.norm(d, axis=1, keepdims=True)
+        moves.append(d)
+
+    def run():
+        pair, system, res = run_pair(tmp_path, case, mode, "float64")
+        out = [(system.f[: case.nlocal].cpu().numpy().copy(), res.energy, tuple(res.virial))]
+        c = case
+        for ago, d in enumerate(moves, start=1):
+            c = moved_case(c, d)
+            r = step_again(pair, system, c, ago)
+            out.append((system.f[: case.nlocal].cpu().numpy().copy(), r.energy, tuple(r.virial)))
+        return out
+
+    first, second = run(), run()
+    for (fa, ea, va), (fb, eb, vb) in zip(first, second):
+        np.testing.assert_array_equal(fa, fb)
+        assert ea == eb and va == vb
