@@ -320,8 +320,9 @@ def run_ljx(args):
     kname = {"density": (f"k_density_groups_full_{precision}" if cached
                          else f"k_density_full_{precision}"),
              "force": f"k_force_rows_full_{precision}"}[kernel]
-    # The committed DRAM captures are of the C3 kernels (full list, newton off).
-    traffic = profile_traffic(kname) if args.config == "c3" else None
+    # Committed DRAM captures: the C3 kernels by name, the C5 ones as "c5:<name>".
+    traffic = {"c3": profile_traffic(kname),
+               "c5": profile_traffic(f"c5:{kname}")}.get(args.config)
 
     total_atoms, energy_total = nlocal, res.energy
     if world > 1:
