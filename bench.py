@@ -174,6 +174,22 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def profile_l1(kernel: str):
+    """Measured L1 data-pipe (LSU wavefront) utilisation of `kernel` from the committed ncu
+    summary, if present: the resource that bounds the gather kernels."""
+    path = ROOT / "profiles" / "l1_wavefronts.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
 def profile_traffic(kernel: str):
     """DRAM bytes per launch of `kernel` from the committed ncu summary, if present."""
     path = ROOT / "profiles" / "dram_traffic.txt"
@@ -323,6 +339,7 @@ def run_ljx(args):
     # Committed DRAM captures: the C3 kernels by name, the C5 ones as "c5:<name>".
     traffic = {"c3": profile_traffic(kname),
                "c5": profile_traffic(f"c5:{kname}")}.get(args.config)
+    l1 = {"c3": profile_l1(kname), "c5": profile_l1(f"c5:{kname}")}.get(args.config)
 
     total_atoms, energy_total = nlocal, res.energy
     if world > 1:
@@ -365,6 +382,10 @@ def run_ljx(args):
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "algorithmic_bytes": kbytes, "traffic": traffic,
+                     "limiter": {"resource": "L1 data pipe (LSU wavefronts): random gathers of "
+                                             "positions and spline rows",
+                                 "frac": l1, "source": "ncu capture of the same kernel on its "
+                                                       "small case (profiles/l1_wavefronts.txt)"},
                      "bytes_basis": "per-step algorithmic bytes of the reference's data flow "
                                     "(list read every step); with the candidate cache the list "
                                     "is read only at rebuilds, so this is an effective bandwidth"
