@@ -351,7 +351,8 @@ def run_ljx(args):
         energy_total = float(t.item())
     neigh_ms = time_list_build(torch, decomp["lists"], system.x, stream)
     e2e = None if args.skip_extras else run_e2e(torch, system, core, args, world,
-                                                 decomp["lists"], total_atoms)
+                                                 decomp["lists"], total_atoms,
+                                                 decomp.get("ghosts"))
     value = total_atoms * args.steps / elapsed
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -464,8 +465,11 @@ def setup_single(ljx, cfg, cells, precision):
     builder = ljx.synth.DeviceListBuilder(x_all, nlocal, CUTOFF + SKIN, half=cfg["half"])
     system.list = builder.build(x)
     system.comm = ljx.SelfComm(torch.as_tensor(owner, device="cuda"), nlocal)
+    # Ghost rows as images of owned rows: whole box lengths per dimension (LAMMPS's pbc shift).
+    shift = np.round((x_all[nlocal:] - x_all[owner]) / atoms.box) * atoms.box
+    ghosts = (system.comm.owner, torch.as_tensor(shift, device="cuda"))
     return system, nlocal, nall, {"pair": pair, "parallelism": "single GPU (periodic self-images)",
-                                  "comm_launches": 1, "lists": builder}
+                                  "comm_launches": 1, "lists": builder, "ghosts": ghosts}
 
 
 def setup_decomposed(ljx, cfg, cells, rank, world, precision, local):
@@ -558,23 +562,42 @@ def time_list_build(torch, lists, x, stream, reps=5):
     return start.elapsed_time(stop) / reps
 
 
-def run_e2e(torch, system, core, args, world, lists, total_atoms):
+def run_e2e(torch, system, core, args, world, lists, total_atoms, ghosts=None):
     """Same step through the C ABI with host buffers: H2D of x and D2H of the forces and the
     result every step. Every `rebuild_every`-th step (10 for C3 and C4, every step for C5) the
     neighbor list is rebuilt on the device from the uploaded positions (ljx_neigh_bin +
     ljx_neigh_build into the same buffers), as LAMMPS-Kokkos builds it on the device."""
+    import ctypes
+
     period = args.rebuild_every if args.rebuild_every > 0 else 10
-    x_host = system.x.cpu().pin_memory()
-    f_host = torch.empty_like(system.f, device="cpu").pin_memory()
+    nlocal, nghost = system.nlocal, system.nghost
+    # One rank owning the whole box: upload the owned positions and fill their periodic images on
+    # the device, as LAMMPS's comm does. Slabs (N > 1) upload every row: their ghosts come from
+    # the neighbors. Only owned forces come back (ghost forces are folded into them with newton
+    # on, unused with newton off).
+    owned_only = ghosts is not None
+    x_host = (system.x[:nlocal] if owned_only else system.x).cpu().pin_memory()
+    f_host = torch.empty_like(system.f[:nlocal], device="cpu").pin_memory()
     stream = torch.cuda.current_stream()
     steps = max(3, min(args.steps, 10))
+    lib = package().abi.load()
 
     def one(k):
-        system.x.copy_(x_host, non_blocking=True)
+        if owned_only:
+            system.x[:nlocal].copy_(x_host, non_blocking=True)
+            owner, shift = ghosts
+            st = lib.ljx_ghost_positions(ctypes.c_void_p(stream.cuda_stream),
+                                         ctypes.c_void_p(system.x.data_ptr()), nlocal, nghost,
+                                         ctypes.c_void_p(owner.data_ptr()),
+                                         ctypes.c_void_p(shift.data_ptr()))
+            if st != 0:
+                raise RuntimeError(f"ljx_ghost_positions failed ({st})")
+        else:
+            system.x.copy_(x_host, non_blocking=True)
         if k % period == 0:
             lists.launch(system.x, stream)
         core(k % period if args.rebuild_every > 0 else -1)  # ends with the result read (a sync)
-        f_host.copy_(system.f, non_blocking=True)
+        f_host.copy_(system.f[:nlocal], non_blocking=True)
         torch.cuda.current_stream().synchronize()        # forces on the host
         return x_host.numel() * 8
 
@@ -596,6 +619,8 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms):
     value = total_atoms * steps / elapsed
     return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d / steps,
             "d2h_bytes_per_step": f_host.numel() * 8 + 9 * 8, "steps": steps,
+            "x_upload": ("owned rows; periodic images filled on the device (ljx_ghost_positions)"
+                         if owned_only else "owned and ghost rows"),
             "list": ("rebuilt on the device every step from the uploaded positions" if period == 1
                      else f"rebuilt on the device every {period}th step from the uploaded "
                           "positions")}
