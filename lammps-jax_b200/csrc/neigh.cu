@@ -121,6 +121,8 @@ k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, G
   __shared__ int s_row[kNeighWarps][kRowsPerPass][kRowCap];
   __shared__ double s_xi[kNeighWarps][kRowsPerPass][3];
   __shared__ int s_i[kNeighWarps][kRowsPerPass];
+  __shared__ int s_start[kNeighWarps][32];  // stencil row q: first entry in bin_atoms
+  __shared__ int s_off[kNeighWarps][32];    // stencil row q: offset in the candidate stream
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
   const long long nbins = static_cast<long long>(g.nb[0]) * g.nb[1] * g.nb[2];
@@ -152,54 +154,77 @@ k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, G
       }
       __syncwarp();
       int count[kRowsPerPass] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int dz = -2; dz <= 2; ++dz) {
-        const int cz = bz + dz;
-        if (cz < 0 || cz >= g.nb[2]) continue;
-        for (int dy = -2; dy <= 2; ++dy) {
-          const int cy = by + dy;
-          if (cy < 0 || cy >= g.nb[1]) continue;
-          // Bins wider than cutoff / 2 can put a whole (dy, dz) row of bins out of range.
-          const double gy = (dy > 1 ? dy - 1 : (dy < -1 ? -dy - 1 : 0)) * g.bin;
-          const double gz = (dz > 1 ? dz - 1 : (dz < -1 ? -dz - 1 : 0)) * g.bin;
-          if (gy * gy + gz * gz > cutsq * (1.0 + 1e-9)) continue;
-          // The bins bx-2 .. bx+2 of this row are consecutive, so their atoms are one range.
+      // The 25 (dy, dz) rows of the stencil, in (dz, dy) order, one per lane: the bins
+      // bx-2 .. bx+2 of a row are consecutive, so their atoms are one range of bin_atoms. The
+      // ranges are walked as one stream of candidates, 32 at a time, so no batch is left mostly
+      // empty at the end of a short range (about 33 atoms per range at solid densities).
+      int start = 0, len = 0;
+      if (lane < 25) {
+        const int dz = lane / 5 - 2, dy = lane % 5 - 2;
+        const int cz = bz + dz, cy = by + dy;
+        // Bins wider than cutoff / 2 can put a whole (dy, dz) row of bins out of range.
+        const double gy = (dy > 1 ? dy - 1 : (dy < -1 ? -dy - 1 : 0)) * g.bin;
+        const double gz = (dz > 1 ? dz - 1 : (dz < -1 ? -dz - 1 : 0)) * g.bin;
+        if (cz >= 0 && cz < g.nb[2] && cy >= 0 && cy < g.nb[1] &&
+            !(gy * gy + gz * gz > cutsq * (1.0 + 1e-9))) {
           const long long row0 = (static_cast<long long>(cz) * g.nb[1] + cy) * g.nb[0];
-          const int c0 = bin_start[row0 + max(bx - 2, 0)];
-          const int c1 = bin_start[row0 + min(bx + 2, g.nb[0] - 1) + 1];
-          for (int s0 = c0; s0 < c1; s0 += 32) {
-            int j = -1;
-            double xj = 0, yj = 0, zj = 0;
-            if (s0 + lane < c1) {
-              j = bin_atoms[s0 + lane];
-              xj = x[3 * j];
-              yj = x[3 * j + 1];
-              zj = x[3 * j + 2];
-            }
+          start = bin_start[row0 + max(bx - 2, 0)];
+          len = bin_start[row0 + min(bx + 2, g.nb[0] - 1) + 1] - start;
+        }
+      }
+      int incl = len;
 #pragma unroll
-            for (int r = 0; r < kRowsPerPass; ++r) {
-              if (r >= m) continue;  // m is the same for every lane
-              const int i = is[r];
-              const double ex = xis[r][0] - xj, ey = xis[r][1] - yj, ez = xis[r][2] - zj;
-              bool keep = j >= 0 && j != i && ex * ex + ey * ey + ez * ez < cutsq;
-              if (keep && half) {
-                if (j < nlocal) {
-                  keep = j > i;
-                } else {
-                  const double zi = xis[r][2], yi = xis[r][1], xi = xis[r][0];
-                  keep = !(zj < zi || (zj == zi && (yj < yi || (yj == yi && xj < xi))));
-                }
-              }
-              const unsigned mk = __ballot_sync(0xffffffffu, keep);
-              if (keep) {
-                const int slot = count[r] + __popc(mk & below);
-                if (slot < kRowCap)
-                  rows[r][slot] = j;
-                else if (slot < maxneigh)
-                  neighbors[i + static_cast<long long>(slot) * stride] = j;
-              }
-              count[r] += __popc(mk);
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int total = __shfl_sync(0xffffffffu, incl, 31);
+      s_start[warp][lane] = start;
+      s_off[warp][lane] = incl - len;
+      __syncwarp();
+      for (int s0 = 0; s0 < total; s0 += 32) {
+        int j = -1;
+        double xj = 0, yj = 0, zj = 0;
+        const int k = s0 + lane;
+        if (k < total) {
+          // The stencil row holding candidate k: the last row whose offset is <= k (empty
+          // rows share their offset with the next one, so they are never the last).
+          int lo = 0, hi = 24;
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_off[warp][mid] <= k)
+              lo = mid;
+            else
+              hi = mid - 1;
+          }
+          j = bin_atoms[s_start[warp][lo] + (k - s_off[warp][lo])];
+          xj = x[3 * j];
+          yj = x[3 * j + 1];
+          zj = x[3 * j + 2];
+        }
+#pragma unroll
+        for (int r = 0; r < kRowsPerPass; ++r) {
+          if (r >= m) continue;  // m is the same for every lane
+          const int i = is[r];
+          const double ex = xis[r][0] - xj, ey = xis[r][1] - yj, ez = xis[r][2] - zj;
+          bool keep = j >= 0 && j != i && ex * ex + ey * ey + ez * ez < cutsq;
+          if (keep && half) {
+            if (j < nlocal) {
+              keep = j > i;
+            } else {
+              const double zi = xis[r][2], yi = xis[r][1], xi = xis[r][0];
+              keep = !(zj < zi || (zj == zi && (yj < yi || (yj == yi && xj < xi))));
             }
           }
+          const unsigned mk = __ballot_sync(0xffffffffu, keep);
+          if (keep) {
+            const int slot = count[r] + __popc(mk & below);
+            if (slot < kRowCap)
+              rows[r][slot] = j;
+            else if (slot < maxneigh)
+              neighbors[i + static_cast<long long>(slot) * stride] = j;
+          }
+          count[r] += __popc(mk);
         }
       }
       __syncwarp();
