@@ -94,14 +94,6 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def workload(cells, seed=2024):
-    ljx = package()
-    atoms = ljx.synth.fcc(cells, A_CU, jitter=JITTER, seed=seed)
-    x_all, owner = ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)
-    types_all = np.ones(len(x_all), np.int32)
-    return atoms, x_all, owner, types_all
-
-
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons during the timed region."""
 
@@ -626,30 +618,50 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms, ghosts=None):
                           "positions")}
 
 
-def cpu_baseline(args, sample_cells=(40, 40, 40), steps=None):
+def reference_sample(ljx, oracle, args):
+    """A bounded CPU sample of the bench workload for the oracle: a 40^3-cell replica of the C3 or
+    C4 crystal (the same lattice, species, potential, cutoffs and list kind) or one 32,000-atom
+    tile of the C5 liquid. Returns (one_step, atoms, description)."""
+    cfg = CONFIGS[args.config]
+    if cfg.get("liquid"):
+        atoms = liquid_atoms(ljx, cfg, 20)
+        what = "one 32,000-atom tile of the C5 liquid"
+    else:
+        n = 40
+        tf = _types_fn(cfg)
+        atoms = ljx.synth.fcc((n, n, n), cfg["lattice"], jitter=JITTER, seed=7,
+                              types=tf(4 * n ** 3, 2025) if tf else None)
+        what = f"{n}^3-cell replica of the {args.config.upper()} crystal"
+    x_all, owner = ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)
+    types_all = np.concatenate([atoms.types, atoms.types[owner]]).astype(np.int32)
+    nlocal = len(atoms.x)
+    tables = oracle.parse_setfl_text(ljx.synth.synthetic_setfl(cfg["elements"]))
+    lst = oracle.build_list(x_all, nlocal, CUTOFF + SKIN, half=cfg["half"])
+    mode = "half-unique" if cfg["half"] else "rows-full"
+
+    def one_step():
+        oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode=mode,
+                        precision=args.precision)
+
+    return one_step, nlocal, f"{what} ({nlocal} atoms, {mode}, {args.precision})"
+
+
+def cpu_baseline(args, steps=2):
     """The CPU restatement (oracle, all host threads) on a bounded replica of the workload."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
     oracle.lib()
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
-    ljx = package()
-    atoms, x_all, owner, types_all = workload(sample_cells, seed=7)
-    nlocal = len(atoms.x)
-    tables = oracle.parse_setfl_text(ljx.synth.synthetic_setfl(("Cu",)))
-    lst = oracle.build_list(x_all, nlocal, CUTOFF + SKIN, half=False)
-    oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
-                    precision=args.precision)
-    steps = steps or 2
+    one_step, nlocal, what = reference_sample(package(), oracle, args)
+    one_step()
     t0 = time.perf_counter()
     for _ in range(steps):
-        oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
-                        precision=args.precision)
+        one_step()
     dt = time.perf_counter() - t0
     return {"value": nlocal * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{sample_cells[0]}^3-cell replica of the workload ({nlocal} atoms), "
-                      f"{steps} full steps (pack + density + embedding + exchange + forces + "
-                      "virial), oracle/eam_oracle.c with OpenMP"}
+            "sample": f"{what}: {steps} full steps (pack + density + embedding + exchange + "
+                      "forces + virial), oracle/eam_oracle.c with OpenMP"}
 
 
 def run_reference(args):
@@ -661,32 +673,25 @@ def run_reference(args):
     oracle.lib()
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
-    ljx = package()
-    cells = (40, 40, 40)
-    atoms, x_all, owner, types_all = workload(cells, seed=7)
-    nlocal = len(atoms.x)
-    tables = oracle.parse_setfl_text(ljx.synth.synthetic_setfl(("Cu",)))
-    lst = oracle.build_list(x_all, nlocal, CUTOFF + SKIN, half=False)
+    cfg = CONFIGS[args.config]
+    one_step, nlocal, what = reference_sample(package(), oracle, args)
     steps = max(1, min(args.steps, 5))
     for _ in range(min(args.warmup, 1)):
-        oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
-                        precision=args.precision)
+        one_step()
     t0 = time.perf_counter()
     for _ in range(steps):
-        oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode="rows-full",
-                        precision=args.precision)
+        one_step()
     dt = time.perf_counter() - t0
     value = nlocal * steps / dt
-    sample = (f"40^3-cell replica of the C3 workload ({nlocal} atoms, same lattice, potential, "
-              f"cutoffs and list), {steps} timed steps")
+    sample = f"{what}, {steps} timed steps"
     print(json.dumps({
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": dt / steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None,
         "dtype": "f64" if args.precision == "float64" else "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "C3: Cu fcc, synthetic EAM rc 6.5 A skin 2.0 A, full list, "
-                               "newton off (CPU sample)", "precision": args.precision},
+        "config": {"workload": cfg["title"].format(c=cfg["cells"]) + " (CPU sample)",
+                   "name": args.config, "precision": args.precision},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -717,6 +722,8 @@ def main():
     ap.add_argument("--skip-extras", action="store_true",
                     help="time the device path only (no e2e or CPU-baseline legs); for profiling")
     args = ap.parse_args()
+    if args.precision is None:
+        args.precision = CONFIGS[args.config].get("precision", "float64")
     (ROOT / "gpurun_out").mkdir(exist_ok=True)
     if args.impl == "reference":
         run_reference(args)
