@@ -203,12 +203,8 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
   __shared__ double2 s_xy[kUnionMax];
   __shared__ double2 s_zw[kUnionMax];
   __shared__ int s_j[kUnionMax];
-  __shared__ int s_qs[kWarpsPerBlock][kQueue];
-  __shared__ double s_qr2[kWarpsPerBlock][kQueue];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
-  int *qs = s_qs[warp];
-  double *qr2 = s_qr2[warp];
   const int groups = (p.inum + kGroupRows - 1) / kGroupRows;
   double kept_sum = 0.0;
   int widest = 0;
@@ -244,36 +240,30 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
       T rho = T(0);
       int kept = 0;
       if (cached) {
-        int q = 0;
-        // Write out and evaluate the first n queued candidates (n <= 32), then drop them.
-        auto flush = [&](int n) {
-          __syncwarp();
-          int slot = 0;
+        // About 80 % of a row's cached candidates are kept, so each batch of 32 evaluates its
+        // kept pairs in place: the idle lanes cost little (a gather costs per sector touched,
+        // not per lane) and no queue round trip through shared memory is needed.
+        const int n = p.rcount[row];
+        const unsigned short *slots = p.rslot + static_cast<long long>(row) * p.rcap;
+        for (int base = 0; base < n; base += kWarp) {
+          int slot = 0, j = 0;
+          bool keep = false;
           double r2d = 0.0;
-          if (lane < n) {
-            slot = qs[lane];
-            r2d = qr2[lane];
+          double4 xj = make_double4(0.0, 0.0, 0.0, 0.0);
+          if (base + lane < n) {
+            // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
+            // staged coordinates.
+            slot = slots[base + lane];
+            xj = staged(s_xy, s_zw, slot);
+            j = s_j[slot];
+            r2d = pack_r2(xi, xj);
+            keep = r2d <= p.pack_cutsq && pair_rules(p, i, xi, j, xj);
           }
-          const int rest = q - n;
-          int ts = 0;
-          double tr = 0.0;
-          if (lane < rest) {
-            ts = qs[n + lane];
-            tr = qr2[n + lane];
-          }
-          __syncwarp();
-          if (lane < rest) {
-            qs[lane] = ts;
-            qr2[lane] = tr;
-          }
-          __syncwarp();
-          if (lane < n) {
-            const int j = s_j[slot];
-            const int at = kept + lane;
+          const unsigned m = __ballot_sync(kFull, keep);
+          if (keep) {
+            const int at = kept + __popc(m & below);
             if (at < p.row_cap) crow[at] = j;
             T r2;
-            const double4 xj = staged(s_xy, s_zw, slot);
-            const int sj = static_cast<int>(xj.w);
             if constexpr (sizeof(T) == 8) {
               r2 = r2d;  // the model's double r^2 is the reference's pack r^2
             } else {
@@ -283,38 +273,14 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
             }
             if (r2 < p.model_cutsq) {
               const T r = sqrt(r2);
+              const int sj = static_cast<int>(xj.w);
               rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
               if (MODE == kDensityHalf)
                 atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
             }
           }
-          kept += n;
-          q = rest;
-        };
-        const int n = p.rcount[row];
-        const unsigned short *slots = p.rslot + static_cast<long long>(row) * p.rcap;
-        for (int base = 0; base < n; base += kWarp) {
-          int slot = 0;
-          bool keep = false;
-          double r2d = 0.0;
-          if (base + lane < n) {
-            // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
-            // staged coordinates.
-            slot = slots[base + lane];
-            const double4 xj = staged(s_xy, s_zw, slot);
-            r2d = pack_r2(xi, xj);
-            keep = r2d <= p.pack_cutsq && pair_rules(p, i, xi, s_j[slot], xj);
-          }
-          const unsigned m = __ballot_sync(kFull, keep);
-          if (keep) {
-            const int at = q + __popc(m & below);
-            qs[at] = slot;
-            qr2[at] = r2d;
-          }
-          q += __popc(m);
-          if (q >= kWarp) flush(kWarp);
+          kept += __popc(m);
         }
-        if (q > 0) flush(q);
       } else {
         // Group past capacity: walk the row's list with the exact test.
         const int n = min(listed, p.maxneighs);
