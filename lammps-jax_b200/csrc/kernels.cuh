@@ -397,6 +397,29 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
       T rho = T(0);
       int kept = 0;  // pairs already written out
       int q = 0;     // pairs waiting in the queue
+      // Write out kept pair (i -> j) at `slot` of the compacted row and add its density.
+      auto evaluate = [&](int slot, int j, float r2f) {
+        if (slot < p.row_cap) crow[slot] = j;
+        if (MODE != kCompactOnly) {
+          T r2;
+          int sj;
+          if constexpr (sizeof(T) == 8) {
+            // The model's double r^2 is the reference's pack r^2 (same operands and order).
+            const double4 xj = load4(p.xd4 + j);
+            r2 = pack_r2(xi, xj);
+            sj = static_cast<int>(xj.w);
+          } else {
+            r2 = r2f;
+            sj = static_cast<int>(__ldg(&pos4f[j].w));
+          }
+          if (r2 < p.model_cutsq) {
+            const T r = sqrt(r2);
+            rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+            if (MODE == kDensityHalf)
+              atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+          }
+        }
+      };
       // Write out and evaluate the first `count` queued pairs (count <= 32), then drop them.
       auto flush = [&](int count) {
         __syncwarp();
@@ -419,29 +442,7 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           qr2[lane] = tr2;
         }
         __syncwarp();
-        if (lane < count) {
-          const int slot = kept + lane;
-          if (slot < p.row_cap) crow[slot] = j;
-          if (MODE != kCompactOnly) {
-            T r2;
-            int sj;
-            if constexpr (sizeof(T) == 8) {
-              // The model's double r^2 is the reference's pack r^2 (same operands and order).
-              const double4 xj = load4(p.xd4 + j);
-              r2 = pack_r2(xi, xj);
-              sj = static_cast<int>(xj.w);
-            } else {
-              r2 = r2f;
-              sj = static_cast<int>(__ldg(&pos4f[j].w));
-            }
-            if (r2 < p.model_cutsq) {
-              const T r = sqrt(r2);
-              rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
-              if (MODE == kDensityHalf)
-                atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
-            }
-          }
-        }
+        if (lane < count) evaluate(kept + lane, j, r2f);
         kept += count;
         q = rest;
       };
@@ -469,13 +470,22 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           }
         }
         const unsigned m = __ballot_sync(kFull, keep);
-        if (keep) {
-          const int at = q + __popc(m & below);
-          qj[at] = j;
-          qr2[at] = r2f;
+        if constexpr (sizeof(T) == 4) {
+          // Float runs evaluate kept pairs in place: their evaluation gathers only the species
+          // word, so idle lanes cost less than the queue's shared-memory round trip.
+          if (keep) evaluate(kept + __popc(m & below), j, r2f);
+          kept += __popc(m);
+        } else {
+          // Double runs gather each kept pair's 32-byte position again; the queue runs that
+          // gather and the spline at full lane occupancy.
+          if (keep) {
+            const int at = q + __popc(m & below);
+            qj[at] = j;
+            qr2[at] = r2f;
+          }
+          q += __popc(m);
+          if (q >= kWarp) flush(kWarp);
         }
-        q += __popc(m);
-        if (q >= kWarp) flush(kWarp);
       }
       if (q > 0) flush(q);
       if (MODE != kCompactOnly) {
