@@ -36,11 +36,10 @@ constexpr int kQueue = 64;
 #else
 #define LJX_DENSITY_BOUNDS __launch_bounds__(kBlock)
 #endif
-#if LJX_FORCE_MIN_BLOCKS > 0
-#define LJX_FORCE_BOUNDS __launch_bounds__(kBlock, LJX_FORCE_MIN_BLOCKS)
-#else
-#define LJX_FORCE_BOUNDS __launch_bounds__(kBlock)
-#endif
+// The force pass: 4 blocks of 256 per SM (64 registers); the double half-list variant, which
+// spills at 64, runs 3 (80 registers) and is faster for it.
+#define LJX_FORCE_BOUNDS \
+  __launch_bounds__(kBlock, (sizeof(T) == 8 && MODE == kHalf) ? 3 : LJX_FORCE_MIN_BLOCKS)
 
 enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2 };
 // Force distribution modes.
@@ -626,10 +625,42 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
     T fx = T(0), fy = T(0), fz = T(0);
     if (n <= p.row_cap) {
       const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
-      for (int k = lane; k < n; k += kWarp) {
-        const int j = crow[k];
-        eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, load_pos(p, j),
-                                  kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
+      if constexpr (sizeof(T) == 8) {
+        // (Pipelining as below spills at 64 registers in double runs and loses.)
+        for (int k = lane; k < n; k += kWarp) {
+          const int j = crow[k];
+          eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, load_pos(p, j),
+                                    kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
+        }
+      } else {
+        // Float runs are software-pipelined by one pair: the next pair's position and F' gathers
+        // are issued before the current pair's spline lookups, so two dependent chains overlap
+        // per lane.
+        int k = lane;
+        int j = 0;
+        V pj = V{};
+        T fpj = T(0);
+        if (k < n) {
+          j = crow[k];
+          pj = load_pos(p, j);
+          if (kNeedFpj) fpj = __ldg(p.fp + j);
+        }
+        while (k < n) {
+          const int k2 = k + kWarp;
+          int j2 = 0;
+          V pj2 = V{};
+          T fpj2 = T(0);
+          if (k2 < n) {
+            j2 = crow[k2];
+            pj2 = load_pos(p, j2);
+            if (kNeedFpj) fpj2 = __ldg(p.fp + j2);
+          }
+          eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v);
+          k = k2;
+          j = j2;
+          pj = pj2;
+          fpj = fpj2;
+        }
       }
     } else {
       const double4 xi = load4(p.xd4 + i);
