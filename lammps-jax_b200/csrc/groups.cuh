@@ -211,6 +211,25 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
   for (int g = blockIdx.x; g < groups; g += gridDim.x) {
     const int count = p.gcount[g];
     const bool cached = count <= p.gcap;
+    // The warp's row and its first 32 candidate slots do not depend on the staged union: they
+    // are loaded before the staging barrier, so their latency overlaps the staging gathers.
+    // (rslot holds rcap >= 32 entries per row; slots past the row's count are not used.)
+    const int row = g * kGroupRows + warp;
+    int i = -1, listed = 0, n = 0;
+    unsigned short slot0 = 0;
+    double4 xi = make_double4(0.0, 0.0, 0.0, 0.0);
+    if (row < p.inum) {
+      i = p.ilist[row];
+      if (i >= p.max_atoms) i = -1;
+    }
+    if (i >= 0) {
+      listed = p.numneigh[i];
+      xi = load4(p.xd4 + i);
+      if (cached) {
+        n = p.rcount[row];
+        slot0 = p.rslot[static_cast<long long>(row) * p.rcap + lane];
+      }
+    }
     if (cached) {
       const int *atoms = p.gatom + static_cast<long long>(g) * p.gcap;
       for (int t = threadIdx.x; t < count; t += kBlock) {
@@ -222,17 +241,9 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
       }
     }
     __syncthreads();
-    const int row = g * kGroupRows + warp;
-    int i = -1;
-    if (row < p.inum) {
-      i = p.ilist[row];
-      if (i >= p.max_atoms) i = -1;
-      if (i < 0 && lane == 0) p.ccount[row] = 0;
-    }
+    if (row < p.inum && i < 0 && lane == 0) p.ccount[row] = 0;
     if (i >= 0) {
-      const int listed = p.numneigh[i];
       widest = max(widest, listed);
-      const double4 xi = load4(p.xd4 + i);
       const float fix = static_cast<float>(xi.x), fiy = static_cast<float>(xi.y),
                   fiz = static_cast<float>(xi.z);
       const int si = static_cast<int>(xi.w);
@@ -243,7 +254,6 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
         // About 80 % of a row's cached candidates are kept, so each batch of 32 evaluates its
         // kept pairs in place: the idle lanes cost little (a gather costs per sector touched,
         // not per lane) and no queue round trip through shared memory is needed.
-        const int n = p.rcount[row];
         const unsigned short *slots = p.rslot + static_cast<long long>(row) * p.rcap;
         for (int base = 0; base < n; base += kWarp) {
           int slot = 0, j = 0;
@@ -253,7 +263,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
           if (base + lane < n) {
             // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
             // staged coordinates.
-            slot = slots[base + lane];
+            slot = base == 0 ? slot0 : slots[base + lane];
             xj = staged(s_xy, s_zw, slot);
             j = s_j[slot];
             r2d = pack_r2(xi, xj);
