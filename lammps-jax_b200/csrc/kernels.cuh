@@ -614,11 +614,31 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
   double e = 0.0;
   double v[6] = {0, 0, 0, 0, 0, 0};
   constexpr bool kNeedFpj = FORCES && MODE != kGhost;
-  for (int row = blockIdx.x * kWarpsPerBlock + warp; row < p.inum;
-       row += gridDim.x * kWarpsPerBlock) {
-    const int i = p.ilist[row];
+  // Float runs and the half-list mode (80 registers) load the next row's atom and kept count
+  // one row ahead, so a row's dependent loads (atom -> position and F') start without waiting
+  // on the list. The double full-list modes would spill at 64 registers, and lose.
+  constexpr bool kAhead = sizeof(T) == 4 || MODE == kHalf;
+  const int stride = gridDim.x * kWarpsPerBlock;
+  int row = blockIdx.x * kWarpsPerBlock + warp;
+  int next_i = 0, next_n = 0;
+  if (kAhead && row < p.inum) {
+    next_i = p.ilist[row];
+    next_n = p.ccount[row];
+  }
+  for (; row < p.inum; row += stride) {
+    int i, n;
+    if constexpr (kAhead) {
+      i = next_i;
+      n = next_n;
+      if (row + stride < p.inum) {
+        next_i = p.ilist[row + stride];
+        next_n = p.ccount[row + stride];
+      }
+    } else {
+      i = p.ilist[row];
+      n = p.ccount[row];
+    }
     if (i >= p.max_atoms) continue;
-    const int n = p.ccount[row];
     const V pi = load_pos(p, i);
     const int si = static_cast<int>(pi.w);
     const T fpi = FORCES ? p.fp[i] : T(0);
