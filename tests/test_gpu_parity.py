@@ -136,6 +136,60 @@ def test_eam_matches_oracle(tmp_path, oracle, mode, precision, elements):
     np.testing.assert_allclose(rho, ref.rho[: case.nlocal].astype(np.float64), rtol=rtol)
 
 
+def funcfl_text(nrho=2000, nr=2000, cutoff=6.5):
+    """A single-element funcfl table (LAMMPS pair_style eam format): F(rho), the effective charge
+    Z(r) (r*phi = 27.2 * 0.529 * Z^2) and rho(r), smooth and zero at the cutoff."""
+    ljx = load_package()
+    synth = ljx.synth
+    dr = cutoff / (nr - 1)
+    r = np.arange(nr) * dr
+    rho_e = synth.fcc_shell_density("Cu", cutoff)
+    drho = 3.0 * rho_e / (nrho - 1)
+    rho = np.arange(nrho) * drho
+    embed = -3.54 * np.sqrt(rho / rho_e) + 0.15 * (rho - rho_e) ** 2
+    z = 1.1 * np.exp(-1.2 * (r - 2.2)) * synth.taper(r, cutoff)
+    lines = ["funcfl table for the parity tests", "29 63.546 3.615 fcc",
+             f"{nrho} {drho!r} {nr} {dr!r} {cutoff!r}"]
+    values = np.concatenate([embed, z, synth.density_fn("Cu", r, cutoff)])
+    lines += [" ".join(f"{v:.17g}" for v in values[k:k + 5]) for k in range(0, len(values), 5)]
+    return "\n".join(lines) + "\n"
+
+
+@pytest.mark.parametrize("mode", ["rows-full", "ghost", "half-unique"])
+def test_funcfl_bundle_matches_oracle(tmp_path, oracle, mode):
+    """A funcfl bundle (pair_style eam tables, eam.py:233-262) through the same engine: forces,
+    energy and virial against the oracle with the oracle's own funcfl reader."""
+    ljx = load_package()
+    text = funcfl_text()
+    case = eam_case(cells=(5, 5, 5), seed=71, nr=100, nrho=100)  # geometry; tables replaced
+    newton, half = MODE_SETUP[mode]
+    kwargs = dict(potential=ljx.bundle.funcfl_potential(text, "Cu"),
+                  max_atoms=len(case.x_all) + 64, max_edges=(len(case.x_all) + 64) * 128,
+                  cutoff=case.cutoff, unit_style="metal", precision="float64", n_species=1,
+                  force_output="atom-force")
+    if mode == "ghost":
+        kwargs.update(newton="on")
+    elif mode == "rows-full":
+        kwargs.update(newton="off", comm=True)
+    else:
+        kwargs.update(newton="on", comm=True, half_edges=True)
+    path = tmp_path / f"funcfl_{mode}.json"
+    ljx.write_bundle(path, **kwargs)
+    system = device_system(case, newton=newton, half=half)
+    pair = ljx.PairJax(device=0)
+    pair.coeff(system, "*", "*", str(path))
+    pair.init_style(system)
+    res = pair.compute(system, eflag=True, vflag=True)
+    if newton:
+        system.comm.reverse_forces(system.f)
+    torch.cuda.synchronize()
+    (tmp_path / "Cu.eam").write_text(text)
+    tables = oracle.load_funcfl(tmp_path / "Cu.eam")
+    ref = oracle.eam_step(tables, case.x_all, case.types_all, case.nlocal, case.owner,
+                          host_list(system.list), mode=mode, precision="float64")
+    assert_parity(res, system, ref, "float64", case)
+
+
 def test_eam_scale_and_extrapolation(tmp_path, oracle):
     # Compressed lattice: densities run past rhomax, so F(rho) extrapolates linearly.
     case = eam_case(cells=(5, 5, 5), a=2.9, jitter=0.05, seed=19, nr=2000, nrho=2000)
