@@ -329,10 +329,11 @@ __device__ __forceinline__ bool keep_pair(const Step<T> &p, const FilterBand &ba
 // staged in shared memory: with the Kokkos LayoutLeft list, slot s of 8 consecutive rows is one
 // 32-byte sector, so the staging load is coalesced where a warp walking one row directly would
 // touch a different cache line per lane. Each warp then filters its row 32 slots at a time
-// (reference distance test and pairing rules), and a ballot appends the kept pairs to a
-// per-warp queue in shared memory; every 32 queued pairs are written out as one coalesced
-// segment of the compacted row and evaluated by all 32 lanes together (sqrt + density spline),
-// so the floating-point work runs at full lane occupancy instead of at the ~40% keep rate.
+// (reference distance test and pairing rules). In double runs a ballot appends the kept pairs
+// to a per-warp queue in shared memory; every 32 queued pairs are written out as one coalesced
+// segment of the compacted row and evaluated by all 32 lanes together (32-byte position gather,
+// sqrt, density spline), so that work runs at full lane occupancy instead of at the ~40% keep
+// rate. Float runs gather only a species word per kept pair and evaluate kept pairs in place.
 template <typename T, int MODE>
 __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
 {
