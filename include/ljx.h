@@ -244,10 +244,13 @@ ljx_status ljx_halo_reverse_self(void *stream, void *rows, int width, int elem_b
  * virial[6] (both times `scale`), kept pairs, widest list row) and the scratch is a fixed
  * LJX_NOALLOC_BYTES device array inside the library, held by every GPU that loads it until the
  * process exits. nlocal + nghost (and inum) must not exceed LJX_NOALLOC_MAX_ATOMS; larger
- * systems get LJX_ERR_CAPACITY before anything is launched. The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress, once per device): make that first call
- * before any stream capture. Calls share the one array, so calls that overlap on the GPU (other
- * streams, other host threads) race; serialize them. Nothing here calls cudaMalloc or cudaFree.
+ * systems get LJX_ERR_CAPACITY before anything is launched. List entries (rows or neighbors) at
+ * or past nlocal + nghost are skipped. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, once per device): make that first call before any stream
+ * capture, and do not call this entry point again on a device the process has reset
+ * (cudaDeviceReset), since the address belongs to the old context. Calls share the one array,
+ * so calls that overlap on the GPU (other streams, other host threads) race; serialize them.
+ * Nothing here calls cudaMalloc or cudaFree.
  * force_layout/newton_pair select the distribution exactly as for an lj/cut bundle.
  * ------------------------------------------------------------------------------------------- */
 #define LJX_NOALLOC_MAX_ATOMS 32768

@@ -34,6 +34,9 @@ void *g_address[64] = {};
 
 // Device address of g_scratch on the current device, looked up once per device. In host code
 // the name g_scratch is only a host-side stand-in, so kernels are always handed this address.
+// The cached address belongs to the device's primary context: after cudaDeviceReset the next
+// context may place the array elsewhere, so a process that resets a device must not call this
+// entry point on that device again.
 ljx_status scratch_address(int device, unsigned char **out)
 {
   if (device < 0 || device >= 64) return LJX_ERR_INVALID;
@@ -75,7 +78,9 @@ ljx_status run(cudaStream_t s, unsigned char *scratch, const ljx_atoms *a, const
   p.n_species = 1;
   p.pack_cutsq = cutoff * cutoff;
   p.model_cutsq = static_cast<T>(cutoff * cutoff);
-  p.max_atoms = kMaxAtoms;
+  // Rows past nall hold whatever an earlier call (possibly of another system) left in the shared
+  // array, so list indices >= nall are dropped exactly as indices past an engine's capacity are.
+  p.max_atoms = p.nall;
   p.scale = scale;
   p.lj_four_eps = static_cast<T>(4.0 * epsilon);
   p.lj_sigma_sq = static_cast<T>(sigma * sigma);
@@ -128,8 +133,10 @@ extern "C" ljx_status ljx_lj_force_noalloc(void *stream, const ljx_atoms *atoms,
   unsigned char *scratch = nullptr;
   const ljx_status st = scratch_address(device, &scratch);
   if (st != LJX_OK) return st;
-  int sm_count = 148;
-  cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device);
+  int sm_count = 0;
+  if (cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      sm_count <= 0)
+    return LJX_ERR_CUDA;
   // Force distribution of an lj/cut bundle as ljx_force decides it (full list unless newton-on
   // edge forces, which take the half list), with the exporter's per-edge energy weight.
   int mode = ljx::kLjEdgeFull;

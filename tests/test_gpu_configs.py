@@ -6,7 +6,8 @@ Here:
   2.0 A hard core, 64/36 species, half list with newton on (the half-unique communicating export),
   128 edges per atom, float64.
 - C3: Cu fcc 80^3 cells = 2,048,000 atoms with 0.08 A Gaussian jitter, full list, newton off,
-  float64, rebuild state as the bench runs it (candidate cache built this step).
+  in float64 and in float32 (the two precisions C3 names), rebuild state as the bench runs it
+  (candidate cache built this step); forces, energy, virial and the kept count.
 - C5: the edge-pack stress test, a binary Cu-Zr liquid at 1.2x fcc density with a 2.0 A core,
   2,048,000 atoms (a 32,000-atom periodic tile repeated 4x4x4), full list with a 2.0 A skin so
   that about half the listed pairs are masked out, 160 edges per atom, float32, a fresh list.
@@ -23,8 +24,7 @@ import numpy as np
 import pytest
 import torch
 
-from cases import (F64_FORCE_REL, F64_TOTAL_REL, Case, canonical_edges, copy_device, host_list,
-                   write_eam_bundle)
+from cases import F32_FORCE_REL, F64_FORCE_REL, Case, canonical_edges, copy_device, write_eam_bundle
 from conftest import load_package
 from test_gpu_parity import assert_parity, oracle_step
 
@@ -72,7 +72,10 @@ def test_c2_binary_amorphous(tmp_path, oracle):
     assert_parity(res, system, ref, "float64", case)
 
 
-def test_c3_full_size(tmp_path, oracle):
+@pytest.mark.parametrize("precision", ["float64", "float32"])
+def test_c3_full_size(tmp_path, oracle, precision):
+    """C3 at its own size in both precisions it names: forces, energy, virial and the kept count
+    against the oracle, and the momentum sum of the periodic crystal."""
     ljx = load_package()
     synth = ljx.synth
     atoms = synth.fcc((80, 80, 80), 3.615, jitter=0.08, seed=2024)
@@ -81,17 +84,16 @@ def test_c3_full_size(tmp_path, oracle):
     case = Case(synth.synthetic_setfl(("Cu",)), x_all, np.ones(len(x_all), np.int32),
                 len(atoms.x), owner, atoms.box, cutoff, skin, 1)
     assert case.nlocal == 2_048_000
-    system, res = run_case(tmp_path, case, "rows-full", newton=False, half=False)
+    system, res = run_case(tmp_path, case, "rows-full", newton=False, half=False,
+                           precision=precision)
     forces = system.f[: case.nlocal]
     fmax = float(forces.abs().max().item())
     # Momentum: pair forces cancel, so the sum is rounding only (2 M terms of size <= fmax).
+    frel = F64_FORCE_REL if precision == "float64" else F32_FORCE_REL
     total = forces.sum(dim=0).abs().max().item()
-    assert total <= 1e-10 * fmax * case.nlocal ** 0.5
-    ref = oracle_step(oracle, case, system, "rows-full", "float64")
-    ferr = float(np.max(np.abs(forces.cpu().numpy() - ref.forces)))
-    assert ferr <= F64_FORCE_REL * float(np.max(np.abs(ref.forces)))
-    assert res.energy == pytest.approx(ref.energy, rel=F64_TOTAL_REL)
-    assert res.edge_count == ref.count
+    assert total <= frel * fmax * case.nlocal ** 0.5
+    ref = oracle_step(oracle, case, system, "rows-full", precision)
+    assert_parity(res, system, ref, precision, case)
 
 
 C5_DENSITY = 1.2 * 4 / 3.615 ** 3  # 1.2x the synthetic Cu fcc density, atoms/A^3
