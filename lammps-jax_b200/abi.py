@@ -1,4 +1,4 @@
-"""ctypes binding of libljx.so (include/ljx.h, include/ljx_neigh.h).
+"""ctypes binding of libljx.so (include/ljx.h, ljx_neigh.h, ljx_pair.h, ljx_md.h, ljx_halo.h).
 
 The library is the product: there is no Python or CPU fallback. Loading fails loudly when the
 shared object is missing or lacks a declared symbol.
@@ -62,6 +62,22 @@ REDUCE_FN = ctypes.CFUNCTYPE(c_int, c_void_p, POINTER(c_int), c_int)
 class PairHost(Structure):
     _fields_ = [("ctx", c_void_p), ("forward_comm", COMM_FN), ("reverse_comm", COMM_FN),
                 ("allreduce_max", REDUCE_FN)]
+
+
+HALO_ID_BYTES = 128
+HALO_SELF_BY_NCCL = 1
+
+
+class Swap(Structure):
+    _fields_ = [("stage", c_int), ("send_rank", c_int), ("recv_rank", c_int),
+                ("sendlist", c_void_p), ("sendnum", c_int), ("firstrecv", c_int),
+                ("recvnum", c_int)]
+
+
+class ResultAll(Structure):
+    _fields_ = [("energy", c_double), ("virial", c_double * 6), ("edge_count", c_longlong),
+                ("edge_max", c_longlong), ("overflow", c_int), ("widest_row", c_int),
+                ("local_energy", c_double)]
 
 
 EFLAG_GLOBAL, VFLAG_GLOBAL, EFLAG_ATOM, VFLAG_ATOM, EFLAG_ONLY = 1, 2, 4, 8, 16
@@ -138,6 +154,17 @@ SIGNATURES = [
                               c_int]),
     ("ljx_ghost_positions", c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     ("ljx_max_displacement", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    ("ljx_halo_unique_id", c_int, [c_void_p]),
+    ("ljx_halo_create", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, POINTER(c_void_p)]),
+    ("ljx_halo_destroy", None, [c_void_p]),
+    ("ljx_halo_error", c_char_p, [c_void_p]),
+    ("ljx_halo_create_error", c_char_p, []),
+    ("ljx_halo_set_swaps", c_int, [c_void_p, POINTER(Swap), c_int, c_int]),
+    ("ljx_halo_forward", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    ("ljx_halo_reverse", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
+    ("ljx_read_result_all", c_int, [c_void_p, c_void_p, c_void_p, POINTER(ResultAll)]),
+    ("ljx_halo_allreduce_sum", c_int, [c_void_p, c_void_p, c_void_p, c_int]),
+    ("ljx_halo_launches", c_longlong, [c_void_p]),
 ]
 
 _lib: ctypes.CDLL | None = None

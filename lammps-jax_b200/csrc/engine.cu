@@ -19,6 +19,7 @@
 
 #include "bundle.h"
 #include "groups.cuh"
+#include "halo_internal.h"
 #include "kernels.cuh"
 #include "ljx.h"
 
@@ -629,6 +630,22 @@ ljx_status pack_atoms_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a)
   return LJX_OK;
 }
 
+// The collective result's inputs from this rank's step totals (k_finalize's result): slots 0..7
+// are summed over ranks (energy, virial, kept edges), 8..10 max-reduced (kept edges, widest
+// row, capacity overflow), 11 stays local (this rank's energy).
+__global__ void k_result_collect(const double *result, double *out, int duplicate, int matrix,
+                                 double capacity)
+{
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const double edges = result[7] * duplicate;
+  for (int k = 0; k < 7; ++k) out[k] = result[k];
+  out[7] = edges;
+  out[8] = edges;
+  out[9] = result[8];
+  out[10] = (matrix ? result[8] : edges) > capacity ? 1.0 : 0.0;
+  out[11] = result[0];
+}
+
 template <typename S>
 void launch_flat_rows(const char *what, long long items, cudaStream_t s, void (*kernel)(S *, int, const int *, int, int),
                       S *rows, int width, const int *owner, int first, int n)
@@ -968,6 +985,42 @@ ljx_status ljx_read_result(ljx_engine *e, void *stream, ljx_result *out)
       res.overflow = res.widest_row > e->c.max_neighbors;
     else
       res.overflow = res.edge_count > e->c.max_edges;
+    if (out) *out = res;
+    for (int &b : e->step_blocks) b = 0;
+    return LJX_OK;
+  });
+}
+
+ljx_status ljx_read_result_all(ljx_engine *e, ljx_halo *halo, void *stream, ljx_result_all *out)
+{
+  return guarded(e, [&]() -> ljx_status {
+    if (halo == nullptr) return fail(e, LJX_ERR_INVALID, "halo is missing");
+    auto s = static_cast<cudaStream_t>(stream);
+    ljx::PartialSet set{};
+    for (int k = 0; k < 4; ++k) {
+      set.ptr[k] = e->partial(k);
+      set.blocks[k] = e->step_blocks[k];
+    }
+    ljx::k_finalize<<<1, ljx::kBlock, 0, s>>>(set, e->last_scale, e->result);
+    check_launch("k_finalize");
+    const bool matrix = e->c.input_layout == LJX_LAYOUT_NEIGHBOR_MATRIX;
+    const double capacity = matrix ? e->c.max_neighbors : e->c.max_edges;
+    k_result_collect<<<1, 32, 0, s>>>(e->result, ljx::halo_scalars(halo), e->last_duplicate,
+                                      matrix ? 1 : 0, capacity);
+    check_launch("k_result_collect");
+    e->launches += 2;
+    double r[12];
+    std::string why;
+    const ljx_status st = ljx::halo_reduce_fetch(halo, s, 8, 3, 12, r, why);
+    if (st != LJX_OK) return fail(e, st, why);
+    ljx_result_all res{};
+    res.energy = r[0];
+    for (int k = 0; k < 6; ++k) res.virial[k] = r[1 + k];
+    res.edge_count = static_cast<long long>(r[7]);
+    res.edge_max = static_cast<long long>(r[8]);
+    res.widest_row = static_cast<int>(r[9]);
+    res.overflow = r[10] > 0.0 ? 1 : 0;
+    res.local_energy = r[11];
     if (out) *out = res;
     for (int &b : e->step_blocks) b = 0;
     return LJX_OK;

@@ -8,14 +8,23 @@ Reverse (ghosts to owners, adding: rho partials, force rows):
   fold the x/y images into their owners on the same rank, pack the z-ghost rows, one grouped
   NCCL send/recv, add them into the sendlist rows they came from, and zero the z-ghost rows.
 The message order is the same on every rank, so two ranks that are each other's upper and lower
-neighbor (two slabs) match their messages in posting order. The row operations are libljx's
-ljx_comm_* / ljx_halo_*_self kernels (GpuRowOps).
+neighbor (two slabs) match their messages in posting order.
+
+Two transports:
+  NcclHalo      the product path: libljx's ljx_halo (include/ljx_halo.h) with the slab's swap
+                table (slab_swaps); every pack, grouped ncclSend/ncclRecv and unpack is issued
+                by the library on the caller's stream, and the step result is one on-stream
+                NCCL all-reduce (ljx_read_result_all).
+  SlabExchange  the same exchange over a torch.distributed group (any backend, gloo on CPU in the
+                tests), with the row operations behind a small interface (GpuRowOps: libljx's
+                ljx_comm_* / ljx_halo_*_self kernels; host stand-ins in the CPU tests).
 """
 
 from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -158,3 +167,157 @@ class SlabExchange:
         t = torch.tensor(list(values), dtype=torch.int64, device=self.device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
         return [int(v) for v in t.tolist()]
+
+
+def slab_swaps(slab, rank: int, nranks: int):
+    """LAMMPS-style swap table of one slab rank (include/ljx_halo.h), as dicts with host send
+    lists. Stage 0 holds the two z swaps: this rank's top rows (send_up) go to the upper
+    neighbor while the lower neighbor's top rows arrive as the low ghosts, and the mirror
+    image. Stage 1 holds the x/y periodic images of owned and z-ghost rows, a self swap. With
+    one rank both z swaps are self swaps too (the slab is its own neighbor along z)."""
+    up, down = (rank + 1) % nranks, (rank - 1) % nranks
+    first_image = slab.nlocal + slab.n_low + slab.n_up
+    return [
+        dict(stage=0, send_rank=up, recv_rank=down, sendlist=np.asarray(slab.send_up, np.int32),
+             firstrecv=slab.nlocal, recvnum=slab.n_low),
+        dict(stage=0, send_rank=down, recv_rank=up, sendlist=np.asarray(slab.send_down, np.int32),
+             firstrecv=slab.nlocal + slab.n_low, recvnum=slab.n_up),
+        dict(stage=1, send_rank=rank, recv_rank=rank, sendlist=np.asarray(slab.xy_owner, np.int32),
+             firstrecv=first_image, recvnum=len(slab.xy_owner)),
+    ]
+
+
+def apply_swaps(rows_by_rank, swaps_by_rank, forward: bool, zero_ghosts: bool = True):
+    """Host restatement of ljx_halo_forward / ljx_halo_reverse over every rank at once (numpy
+    rows, first axis = atom rows): the semantics the library implements, for tests. Messages
+    from one rank to another within a stage match in posting order."""
+    nranks = len(rows_by_rank)
+    stages = sorted({sw["stage"] for sws in swaps_by_rank for sw in sws})
+
+    def inbox(stage, r, q, src, direction):
+        """Position of swap q among rank r's swaps of `stage` that talk to `src`, and the
+        matching message of `src` (its k-th swap of the stage aimed at r)."""
+        mine = [qq for qq, sw in enumerate(swaps_by_rank[r])
+                if sw["stage"] == stage and sw[direction[0]] == src]
+        theirs = [qq for qq, sw in enumerate(swaps_by_rank[src])
+                  if sw["stage"] == stage and sw[direction[1]] == r]
+        return theirs[mine.index(q)]
+
+    for stage in (stages if forward else stages[::-1]):
+        if forward:
+            sent = {(r, q): rows_by_rank[r][sw["sendlist"]].copy()
+                    for r in range(nranks) for q, sw in enumerate(swaps_by_rank[r])
+                    if sw["stage"] == stage}
+            for r in range(nranks):
+                for q, sw in enumerate(swaps_by_rank[r]):
+                    if sw["stage"] != stage:
+                        continue
+                    src = sw["recv_rank"]
+                    msg = sent[(src, inbox(stage, r, q, src, ("recv_rank", "send_rank")))]
+                    rows_by_rank[r][sw["firstrecv"]:sw["firstrecv"] + sw["recvnum"]] = msg
+        else:
+            back = {}
+            for r in range(nranks):
+                for q, sw in enumerate(swaps_by_rank[r]):
+                    if sw["stage"] != stage:
+                        continue
+                    lo, hi = sw["firstrecv"], sw["firstrecv"] + sw["recvnum"]
+                    back[(r, q)] = rows_by_rank[r][lo:hi].copy()
+                    if zero_ghosts:
+                        rows_by_rank[r][lo:hi] = 0
+            for r in range(nranks):
+                for q, sw in enumerate(swaps_by_rank[r]):
+                    if sw["stage"] != stage:
+                        continue
+                    src = sw["send_rank"]
+                    msg = back[(src, inbox(stage, r, q, src, ("send_rank", "recv_rank")))]
+                    np.add.at(rows_by_rank[r], sw["sendlist"], msg)
+    return rows_by_rank
+
+
+def _broadcast_id(group=None) -> bytes:
+    """One NCCL unique id made on rank 0 and broadcast over the torch.distributed group."""
+    lib = abi.load()
+    payload = [None]
+    if dist.get_rank(group) == 0:
+        buf = (ctypes.c_ubyte * abi.HALO_ID_BYTES)()
+        st = lib.ljx_halo_unique_id(buf)
+        if st != abi.OK:
+            raise abi.LjxError(st, lib.ljx_halo_create_error().decode())
+        payload = [bytes(buf)]
+    dist.broadcast_object_list(payload, src=0, group=group)
+    return payload[0]
+
+
+class NcclHalo:
+    """A libljx NCCL halo (ljx_halo) with a swap table: the multi-GPU exchange of the harness.
+
+    `unique_id` is the NCCL id every rank shares (made and broadcast over the torch.distributed
+    group when omitted). The send lists live on the device for the halo's lifetime."""
+
+    def __init__(self, swaps, rank: int, nranks: int, device: int, unique_id: bytes | None = None,
+                 group=None, timeout_ms: int = 60000, flags: int = 0, max_row_bytes: int = 24):
+        self.lib = abi.load()
+        uid = unique_id if unique_id is not None else _broadcast_id(group)
+        idbuf = (ctypes.c_ubyte * abi.HALO_ID_BYTES).from_buffer_copy(uid)
+        out = ctypes.c_void_p()
+        st = self.lib.ljx_halo_create(idbuf, nranks, rank, device, timeout_ms, flags,
+                                      ctypes.byref(out))
+        if st != abi.OK:
+            raise abi.LjxError(st, self.lib.ljx_halo_create_error().decode())
+        self._h = out
+        self.rank, self.nranks = rank, nranks
+        self.set_swaps(swaps, max_row_bytes)
+
+    def _check(self, st):
+        if st != abi.OK:
+            raise abi.LjxError(st, self.lib.ljx_halo_error(self._h).decode())
+
+    def set_swaps(self, swaps, max_row_bytes: int = 24):
+        self._lists = [torch.as_tensor(np.ascontiguousarray(sw["sendlist"], np.int32),
+                                       device="cuda") for sw in swaps]
+        table = (abi.Swap * max(1, len(swaps)))()
+        for k, (sw, lst) in enumerate(zip(swaps, self._lists)):
+            table[k] = abi.Swap(sw["stage"], sw["send_rank"], sw["recv_rank"], lst.data_ptr(),
+                                int(lst.numel()), sw["firstrecv"], sw["recvnum"])
+        self._check(self.lib.ljx_halo_set_swaps(self._h, table, len(swaps), max_row_bytes))
+
+    @staticmethod
+    def _s(stream=None):
+        return ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
+
+    def forward(self, rows, width: int, elem_bytes: int, stream=None):
+        """Fill every ghost row of `rows` (a device address) from its owner."""
+        self._check(self.lib.ljx_halo_forward(self._h, self._s(stream), ctypes.c_void_p(rows),
+                                              width, elem_bytes))
+
+    def reverse(self, rows, width: int, elem_bytes: int, stream=None):
+        """Add every ghost row into its owner's row, then zero the ghost rows."""
+        self._check(self.lib.ljx_halo_reverse(self._h, self._s(stream), ctypes.c_void_p(rows),
+                                              width, elem_bytes, 1))
+
+    def reverse_forces(self, f: torch.Tensor, stream=None):
+        """LAMMPS's own reverse comm of ghost force rows (newton on)."""
+        self.reverse(f.data_ptr(), 3, 8, stream)
+
+    def result_all(self, engine, stream=None) -> abi.ResultAll:
+        """The step result over all ranks (ljx_read_result_all)."""
+        out = abi.ResultAll()
+        st = self.lib.ljx_read_result_all(engine._h, self._h, self._s(stream), ctypes.byref(out))
+        if st != abi.OK:
+            raise abi.LjxError(st, self.lib.ljx_engine_error(engine._h).decode())
+        return out
+
+    def allreduce_sum(self, t: torch.Tensor, stream=None):
+        """In-place sum over ranks of a float64 device tensor."""
+        self._check(self.lib.ljx_halo_allreduce_sum(self._h, self._s(stream),
+                                                    ctypes.c_void_p(t.data_ptr()), t.numel()))
+
+    @property
+    def launches(self) -> int:
+        return int(self.lib.ljx_halo_launches(self._h))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.ljx_halo_destroy(self._h)
+        self._h = None

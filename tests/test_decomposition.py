@@ -7,6 +7,9 @@
 3. Transport: SlabExchange over a real 2-rank gloo process group fills every ghost row with its
    owner's value (forward) and adds every ghost row back into its owner (reverse), with host
    stand-ins for the row operations (on GPUs the ljx_comm_* kernels do them).
+4. Identity: the slabs of every rank count own exactly the atoms of the whole crystal.
+5. The swap table of libljx's NCCL halo, applied with the host restatement of its semantics,
+   fills and folds every ghost row for 1, 2 and 3 ranks.
 """
 
 import os
@@ -179,3 +182,54 @@ def test_slab_exchange_over_gloo(nranks):
     results = manager.dict()
     mp.spawn(_exchange_worker, args=(nranks, free_port(), results), nprocs=nranks, join=True)
     assert dict(results) == {r: (True, True) for r in range(nranks)}
+
+
+@pytest.mark.parametrize("nranks", [1, 2, 3])
+def test_slabs_are_one_crystal_at_every_rank_count(ljx, nranks):
+    """Per-layer seeding: every decomposition owns exactly the atoms of the whole crystal (same
+    coordinates, species and global ids), so runs at different GPU counts compare atom by atom."""
+    cells = (4, 4, 6)
+    whole = ljx.synth.layered_crystal(cells, A, JITTER, SEED, (0.64, 0.36))
+    per = (cells[0], cells[1], cells[2] // nranks)
+    parts = [ljx.synth.slab_decomposition(per, A, JITTER, SEED, r, nranks, CUT,
+                                          fractions=(0.64, 0.36)) for r in range(nranks)]
+    ids = np.concatenate([p.ids for p in parts])
+    x = np.concatenate([p.x[:p.nlocal] for p in parts])
+    t = np.concatenate([p.types[:p.nlocal] for p in parts])
+    o, ow = np.argsort(ids), np.argsort(whole.ids)
+    np.testing.assert_array_equal(ids[o], whole.ids[ow])
+    np.testing.assert_array_equal(x[o], whole.x[ow])
+    np.testing.assert_array_equal(t[o], whole.types[ow])
+
+
+@pytest.mark.parametrize("nranks", [1, 2, 3])
+def test_swap_table_fills_and_folds_every_ghost(ljx, nranks):
+    """The swap table libljx's NCCL halo runs (halo.slab_swaps), applied with the host
+    restatement of ljx_halo_forward/_reverse: forward fills every ghost row with its owner's
+    value; reverse adds every ghost row into its owner and zeroes it."""
+    from lammps_jax_b200.halo import apply_swaps, slab_swaps
+    parts = slabs(ljx, nranks)
+    owners, offsets = combined_owner(parts)
+    swaps = [slab_swaps(p, r, nranks) for r, p in enumerate(parts)]
+    rows = []
+    for r, p in enumerate(parts):
+        v = np.full((len(p.x), 2), -1.0)
+        v[:p.nlocal, 0] = np.arange(p.nlocal) + offsets[r]
+        v[:p.nlocal, 1] = 2.0 * (np.arange(p.nlocal) + offsets[r])
+        rows.append(v)
+    apply_swaps(rows, swaps, forward=True)
+    for r, p in enumerate(parts):
+        np.testing.assert_array_equal(rows[r][p.nlocal:, 0], owners[r])
+        np.testing.assert_array_equal(rows[r][p.nlocal:, 1], 2.0 * owners[r])
+    rows = []
+    for p in parts:
+        v = np.zeros((len(p.x), 2))
+        v[p.nlocal:] = 1.0
+        rows.append(v)
+    apply_swaps(rows, swaps, forward=False)
+    counts = np.bincount(np.concatenate(owners), minlength=int(offsets[-1]))
+    for r, p in enumerate(parts):
+        mine = counts[offsets[r]:offsets[r] + p.nlocal]
+        np.testing.assert_array_equal(rows[r][:p.nlocal, 0], mine)
+        np.testing.assert_array_equal(rows[r][:p.nlocal, 1], mine)
+        assert not np.any(rows[r][p.nlocal:])
