@@ -11,12 +11,17 @@ The neighbor list is built once and held fixed (positions are static across time
 list alone (about 1.9 GB) is larger than the 126 MB L2, so no separate flush is needed.
 
 --impl reference times the CPU restatement of the reference's path (oracle/, OpenMP on all host
-threads) on a bounded sample of the same workload (a 40^3-cell replica) and prints the same line
-with "impl": "reference".
+threads) on the same 2,048,000-atom workload, the same warm-up and timed steps, and prints the
+same line with "impl": "reference".
 
 Multi-GPU runs (torchrun, one rank per GPU) use spatial decomposition along z: every rank owns a
 2,048,000-atom slab of a larger crystal (weak scaling) and exchanges F'(rho) of its boundary
-atoms with its two z-neighbors over NCCL each step.
+atoms with its two z-neighbors each step through libljx's NCCL halo (ljx_halo); the step totals
+and the collective capacity check are one on-stream NCCL all-reduce.
+
+The c3 line also carries a "c4" object: the 16,384,000-atom C4 crystal (the same atoms at every
+GPU count) split over the run's GPUs (strong scaling), with its total energy, virial and a
+sample of forces by global atom id, so runs at different GPU counts compare atom by atom.
 
 --config c4 is the strong-scaling case (16,384,000-atom binary crystal split over the GPUs, half
 list, newton on: reverse rho, forward F'(rho) and reverse force exchanges). --config c5 is the
@@ -166,10 +171,10 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def profile_l1(kernel: str):
-    """Measured L1 data-pipe (LSU wavefront) utilisation of `kernel` from the committed ncu
-    summary, if present: the resource that bounds the gather kernels."""
-    path = ROOT / "profiles" / "l1_wavefronts.txt"
+def profile_entry(name: str, kernel: str):
+    """Value of `kernel` in the committed ncu summary profiles/<name>, or None. These figures
+    come from an earlier one-kernel capture of a smaller case, not from this run."""
+    path = ROOT / "profiles" / name
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
@@ -182,26 +187,161 @@ def profile_l1(kernel: str):
     return None
 
 
-def profile_traffic(kernel: str):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if present."""
-    path = ROOT / "profiles" / "dram_traffic.txt"
-    if not path.exists():
-        return None
-    for line in path.read_text().splitlines():
-        parts = line.split()
-        if len(parts) >= 2 and parts[0] == kernel:
-            try:
-                return float(parts[1])
-            except ValueError:
-                return None
-    return None
+class Case:
+    """One configuration set up on this rank: the LAMMPS stand-in state, the pair style and the
+    exchange (SelfComm on one GPU, libljx's NCCL halo across GPUs)."""
+
+    def __init__(self, ljx, name, precision, world, rank, local, cells=None):
+        import torch
+        cfg = CONFIGS[name]
+        self.name, self.cfg, self.precision = name, cfg, precision
+        self.world, self.rank = world, rank
+        if cfg["strong"]:
+            total = cells or cfg["cells"]
+            if total % world:
+                raise SystemExit(f"--config {name}: {total} z-cells do not split over {world} GPUs")
+            self.cells = (total, total, total // world)
+        else:
+            n = cells or cfg["cells"]
+            self.cells = (n, n, n)
+        if world > 1:
+            setup = setup_decomposed(ljx, cfg, self.cells, rank, world, precision, local)
+        else:
+            setup = setup_single(ljx, cfg, self.cells, precision)
+        self.system, self.nlocal, self.nall, self.decomp = setup
+        self.pair = self.decomp["pair"]
+        self.plan = self.pair.plan
+        self.eng = self.pair.engine
+        self.atoms = self.system.atoms()
+        self.nl = self.system.list.struct()
+        self.fp_rows, self.width, self.elem = self.eng.feature_rows(1)
+        self.rho_rows = self.eng.feature_rows(0)[0]
+        self.halo = self.decomp.get("halo")
+        self.stream = torch.cuda.current_stream()
+        self.tick = 0
+
+    def core(self, ago, mark=lambda k: None):
+        """One pair-style step on device data, with the exchanges the engine's plan asks for.
+        Returns (energy, virial, kept edges, overflow) over all ranks."""
+        s, eng, atoms, nl = self.system, self.eng, self.atoms, self.nl
+        newton = s.newton_pair
+        nl.ago = ago
+        mark(0)
+        eng.pack_atoms(atoms)
+        mark(1)
+        eng.density(atoms, nl, newton)
+        if self.plan.reverse_density:
+            s.comm.reverse(self.rho_rows, self.width, self.elem)
+        mark(2)
+        eng.embed(atoms)
+        mark(3)
+        if self.plan.forward_fp:
+            s.comm.forward(self.fp_rows, self.width, self.elem)
+        mark(4)
+        eng.force(atoms, nl, newton, 1.0)
+        if self.plan.reverse_force:
+            s.comm.reverse_forces(s.f)  # LAMMPS's own reverse comm of ghost forces
+        mark(5)
+        if self.halo is not None:
+            # The collective capacity check and step totals: one NCCL all-reduce on the stream
+            # and one host wait (the pair style's MPI_Allreduce after execution).
+            res = self.halo.result_all(eng)
+        else:
+            res = eng.read_result()
+        out = (res.energy, list(res.virial), res.edge_count, res.overflow)
+        if out[3]:
+            raise RuntimeError("LAMMPS-JAX edge capacity exceeded")
+        mark(6)
+        return out
+
+    def step(self, rebuild_every, events=None):
+        def mark(k):
+            if events is not None:
+                events[k].record(self.stream)
+        # neighbor->ago as LAMMPS reports it with a rebuild every `rebuild_every` steps; the
+        # engine rebuilds its candidate cache on ago == 0 (-1: cache off).
+        ago = self.tick % rebuild_every if rebuild_every > 0 else -1
+        self.tick += 1
+        return self.core(ago, mark)
+
+    def launches(self):
+        return self.eng.launches + (self.halo.launches if self.halo is not None else 0)
+
+    def time(self, steps, warmup, rebuild_every):
+        """Warm up, then time `steps` steps with CUDA events on the launching stream, bracketed
+        by a barrier and a device synchronize; the max over ranks."""
+        import torch
+        import torch.distributed as dist
+        names = ["pack_atoms", "density", "embed", "halo_fp", "force", "result"]
+        self.system.f.zero_()
+        kevents = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(steps)]
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        out = None
+        for _ in range(warmup):
+            out = self.step(rebuild_every)
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier()
+        launches0 = self.launches()
+        start.record(self.stream)
+        for k in range(steps):
+            out = self.step(rebuild_every, kevents[k])
+        stop.record(self.stream)
+        torch.cuda.synchronize()
+        elapsed = start.elapsed_time(stop) / 1e3
+        if self.world > 1:
+            t = torch.tensor([elapsed], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            elapsed = float(t.item())
+        launches = self.launches() - launches0 + steps * self.decomp["extra_launches"]
+        phase = {n: 0.0 for n in names}
+        for ev in kevents:
+            for k, n in enumerate(names):
+                phase[n] += ev[k].elapsed_time(ev[k + 1]) / 1e3
+        return {"elapsed": elapsed, "launches": launches, "result": out,
+                "phase": {n: v / steps for n, v in phase.items()}}
+
+    def total_atoms(self):
+        import torch
+        import torch.distributed as dist
+        if self.world == 1:
+            return self.nlocal
+        t = torch.tensor([self.nlocal], dtype=torch.int64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return int(t.item())
+
+    def clean_forces(self, sample_ids, rebuild_every):
+        """One step from zeroed forces; returns (energy, virial, max |F| over all owned atoms,
+        {global id: force} for the owned atoms among `sample_ids`)."""
+        import torch
+        import torch.distributed as dist
+        self.system.f.zero_()
+        energy, virial, _, _ = self.step(rebuild_every)
+        torch.cuda.synchronize()
+        f = self.system.f[:self.nlocal]
+        fmax = f.abs().max().reshape(1)
+        if self.world > 1:
+            dist.all_reduce(fmax, op=dist.ReduceOp.MAX)
+        ids = self.decomp["ids"]
+        where = np.nonzero(np.isin(ids, sample_ids))[0]
+        rows = (f[torch.as_tensor(where, device="cuda")].cpu().numpy() if len(where)
+                else np.zeros((0, 3)))
+        mine = {int(ids[w]): [float(v) for v in rows[k]] for k, w in enumerate(where)}
+        if self.world > 1:
+            parts = [None] * self.world
+            dist.all_gather_object(parts, mine)
+            mine = {k: v for p in parts for k, v in p.items()}
+        return energy, virial, float(fmax.item()), mine
+
+    def close(self):
+        self.pair.engine.close()
+        if self.halo is not None:
+            self.halo.close()
 
 
-def run_ljx(args):
+def init_ranks():
     import torch
     import torch.distributed as dist
-
-    ljx = package()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -210,114 +350,43 @@ def run_ljx(args):
         import datetime
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=datetime.timedelta(seconds=180))
+    return world, rank, local
+
+
+def run_ljx(args):
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+
+    ljx = package()
+    world, rank, local = init_ranks()
     cfg = CONFIGS[args.config]
     precision = args.precision or cfg.get("precision", "float64")
     if args.rebuild_every is None:
         args.rebuild_every = cfg.get("rebuild_every", 10)
     if cfg.get("one_gpu") and world > 1:
         raise SystemExit(f"--config {args.config} runs on one GPU")
-    if cfg["strong"]:
-        total = args.cells or cfg["cells"]
-        if total % world:
-            raise SystemExit(f"--config {args.config}: {total} z-cells do not split over {world} GPUs")
-        cells = (total, total, total // world)
-    else:
-        n = args.cells or cfg["cells"]
-        cells = (n, n, n)
-    if world > 1:
-        system, nlocal, nall, decomp = setup_decomposed(ljx, cfg, cells, rank, world, precision,
-                                                        local)
-    else:
-        system, nlocal, nall, decomp = setup_single(ljx, cfg, cells, precision)
-    pair = decomp["pair"]
-    plan = pair.plan
-    newton = system.newton_pair
-    stream = torch.cuda.current_stream()
-    eng = pair.engine
-    atoms = system.atoms()
-    nl = system.list.struct()
-    fp_rows, width, elem = eng.feature_rows(1)
-    rho_rows = eng.feature_rows(0)[0]
+    case = Case(ljx, args.config, precision, world, rank, local, args.cells)
+    system, nlocal, nall, decomp = case.system, case.nlocal, case.nall, case.decomp
 
-    names = ["pack_atoms", "density", "embed", "halo_fp", "force", "result"]
-    tick = [0]
+    # The clock samples span the warm-up and the timed steps (both under load); they go to a
+    # temporary file, read back for the line's "clocks".
+    clock_file = Path(tempfile.mkdtemp(prefix="ljx_clocks_")) / f"clocks_rank{rank}.csv"
+    with ClockSampler(local, clock_file) as clocks:
+        timing = case.time(args.steps, args.warmup, args.rebuild_every)
+    elapsed, phase, launches = timing["elapsed"], timing["phase"], timing["launches"]
+    energy_total, _, kept_total, _ = timing["result"]
 
-    def core(ago, mark=lambda k: None):
-        """One pair-style step on device data, with the exchanges the engine's plan asks for."""
-        nl.ago = ago
-        mark(0)
-        eng.pack_atoms(atoms)
-        mark(1)
-        eng.density(atoms, nl, newton)
-        if plan.reverse_density:
-            system.comm.reverse(rho_rows, width, elem)
-        mark(2)
-        eng.embed(atoms)
-        mark(3)
-        if plan.forward_fp:
-            system.comm.forward(fp_rows, width, elem)
-        mark(4)
-        eng.force(atoms, nl, newton, 1.0)
-        if plan.reverse_force:
-            system.comm.reverse_forces(system.f)  # LAMMPS's own reverse comm of ghost forces
-        mark(5)
-        res = eng.read_result()
-        if world > 1:
-            # Collective capacity check, as the pair style's MPI_Allreduce after execution.
-            flags = torch.tensor([res.edge_count, res.overflow], device="cuda")
-            dist.all_reduce(flags, op=dist.ReduceOp.MAX)
-            if int(flags[1].item()):
-                raise RuntimeError("LAMMPS-JAX edge capacity exceeded")
-        mark(6)
-        return res
-
-    def step(events=None):
-        def mark(k):
-            if events is not None:
-                events[k].record(stream)
-        # neighbor->ago as LAMMPS reports it with a rebuild every `rebuild_every` steps; the
-        # engine rebuilds its candidate cache on ago == 0 (-1: cache off).
-        ago = tick[0] % args.rebuild_every if args.rebuild_every > 0 else -1
-        tick[0] += 1
-        return core(ago, mark)
-
-    system.f.zero_()
-    kevents = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # The clock samples span the warm-up and the timed steps (both under load).
-    with ClockSampler(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv") as clocks:
-        for _ in range(args.warmup):
-            res = step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        launches0 = eng.launches
-        start.record(stream)
-        for k in range(args.steps):
-            res = step(kevents[k])
-        stop.record(stream)
-        torch.cuda.synchronize()
-    elapsed = start.elapsed_time(stop) / 1e3
-    if world > 1:
-        t = torch.tensor([elapsed], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t.item())
-    # Our kernels per step: pack_atoms, density, embed, forward exchange, force, finalize.
-    launches = (eng.launches - launches0) + args.steps * decomp["comm_launches"]
-    phase = {n: 0.0 for n in names}
-    for ev in kevents:
-        for k, n in enumerate(names):
-            phase[n] += ev[k].elapsed_time(ev[k + 1]) / 1e3
-    phase = {n: v / args.steps for n, v in phase.items()}
-
-    # Algorithmic bytes per launch (per step) of the two row kernels.
+    # Algorithmic bytes per launch (per step) of the two row kernels, for this rank.
     nn = system.list.numneigh[:nlocal].to(torch.int64)
     listed = int(nn.sum().item())
-    kept = int(res.edge_count)
+    kept_local = kept_total // world
     real = 8 if precision == "float64" else 4
-    bytes_density = 4 * listed + 4 * nlocal * 2 + 32 * nall + 4 * kept + 4 * nlocal + real * nlocal
+    bytes_density = (4 * listed + 4 * nlocal * 2 + 32 * nall + 4 * kept_local + 4 * nlocal +
+                     real * nlocal)
     pos_bytes = 32 if precision == "float64" else 16
-    bytes_force = 8 * nlocal + 4 * kept + pos_bytes * nall + real * nall + 48 * nlocal
+    bytes_force = 8 * nlocal + 4 * kept_local + pos_bytes * nall + real * nall + 48 * nlocal
     kernel = max(("density", "force"), key=lambda n: phase[n])
     kbytes = bytes_density if kernel == "density" else bytes_force
     achieved = kbytes / phase[kernel] / 1e9
@@ -328,23 +397,15 @@ def run_ljx(args):
     kname = {"density": (f"k_density_groups_full_{precision}" if cached
                          else f"k_density_full_{precision}"),
              "force": f"k_force_rows_full_{precision}"}[kernel]
-    # Committed DRAM captures: the C3 kernels by name, the C5 ones as "c5:<name>".
-    traffic = {"c3": profile_traffic(kname),
-               "c5": profile_traffic(f"c5:{kname}")}.get(args.config)
-    l1 = {"c3": profile_l1(kname), "c5": profile_l1(f"c5:{kname}")}.get(args.config)
+    # DRAM bytes and L1 utilisation of this kernel come from committed one-kernel ncu captures
+    # (C3 kernels by name, C5 ones as "c5:<name>"), labelled as such: no profiler runs here.
+    key = {"c3": kname, "c5": f"c5:{kname}"}.get(args.config)
+    traffic = profile_entry("dram_traffic.txt", key) if key else None
+    l1 = profile_entry("l1_wavefronts.txt", key) if key else None
 
-    total_atoms, energy_total = nlocal, res.energy
-    if world > 1:
-        t = torch.tensor([nlocal], dtype=torch.int64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        total_atoms = int(t.item())
-        t = torch.tensor([res.energy], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        energy_total = float(t.item())
-    neigh_ms = time_list_build(torch, decomp["lists"], system.x, stream)
-    e2e = None if args.skip_extras else run_e2e(torch, system, core, args, world,
-                                                 decomp["lists"], total_atoms,
-                                                 decomp.get("ghosts"))
+    total_atoms = case.total_atoms()
+    neigh_ms = time_list_build(torch, decomp["lists"], system.x, case.stream)
+    e2e = None if args.skip_extras else run_e2e(torch, case, args, world, total_atoms)
     value = total_atoms * args.steps / elapsed
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -352,10 +413,11 @@ def run_ljx(args):
         "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None,
         "dtype": "f64" if precision == "float64" else "f32", "data": "synthetic",
         "config": {
-            "workload": cfg["title"].format(c=cells[0]) + f" ({total_atoms:,} atoms in all)",
+            "workload": cfg["title"].format(c=case.cells[0]) + f" ({total_atoms:,} atoms in all)",
             "name": args.config, "total_atoms": total_atoms,
             "atoms_per_gpu": nlocal, "ghosts_per_gpu": nall - nlocal,
-            "listed_pairs_per_atom": listed / nlocal, "kept_edges_per_atom": kept / nlocal,
+            "listed_pairs_per_atom": listed / nlocal,
+            "kept_edges_per_atom": kept_total / total_atoms,
             "precision": precision, "l2": "inputs larger than L2 (neighbor list "
                                            f"{system.list.neighbors.numel() * 4 / 1e9:.2f} GB)",
             "list": ("built once on the device, fixed over timed steps; the engine is told "
@@ -375,10 +437,17 @@ def run_ljx(args):
         "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "algorithmic_bytes": kbytes, "traffic": traffic,
+                     "traffic_source": ("profiles/dram_traffic.txt: dram__bytes_read.sum + "
+                                        "dram__bytes_write.sum of a committed one-kernel ncu "
+                                        "capture of the 256,000-atom case, scaled x8 by owned "
+                                        "atoms to the full launch; not measured in this run"
+                                        if traffic is not None else None),
                      "limiter": {"resource": "L1 data pipe (LSU wavefronts): random gathers of "
                                              "positions and spline rows",
-                                 "frac": l1, "source": "ncu capture of the same kernel on its "
-                                                       "small case (profiles/l1_wavefronts.txt)"},
+                                 "frac": l1,
+                                 "source": "profiles/l1_wavefronts.txt: committed one-kernel ncu "
+                                           "capture of the same kernel on its 256,000-atom case; "
+                                           "not measured in this run"},
                      "bytes_basis": "per-step algorithmic bytes of the reference's data flow "
                                     "(list read every step); with the candidate cache the list "
                                     "is read only at rebuilds, so this is an effective bandwidth"
@@ -389,25 +458,56 @@ def run_ljx(args):
         "energy_per_atom": energy_total / total_atoms,
     }
     if world == 1 and not args.skip_extras and args.config == "c3":
-        line["md"] = run_md(torch, ljx, cfg, cells, precision, args.steps, args.warmup)
+        line["md"] = run_md(torch, ljx, cfg, case.cells, precision, args.steps, args.warmup)
+    line["clocks"] = clocks.summary()
+    case.close()
+    del case, system, decomp
+    torch.cuda.empty_cache()
+    if not args.skip_extras and not args.no_c4 and args.config == "c3":
+        line["c4"] = run_c4(ljx, args, world, rank, local)
+    if world == 1 and not args.skip_extras and args.config == "c3":
         line["cpu_baseline"] = cpu_baseline(args)
-    clocks_summary = clocks.summary()
-    line["clocks"] = clocks_summary
     if world > 1:
         dist.barrier()
     if rank == 0:
         print(json.dumps(line), flush=True)
-    pair.engine.close()
     if world > 1:
-        decomp["close"]()
         dist.destroy_process_group()
 
 
-def _types_fn(cfg):
-    if cfg["fractions"] is None:
-        return None
-    ljx = package()
-    return lambda n, seed: ljx.synth.substitutional(n, cfg["fractions"], seed=seed)
+C4_SAMPLES = 16
+
+
+def run_c4(ljx, args, world, rank, local):
+    """The north-star strong-scaling case beside the headline: C4's 16,384,000-atom binary
+    crystal (160^3 cells, one identical system at every GPU count, fcc_layers) split into
+    z-slabs over the GPUs of this run, timed like the headline, with the totals and a sample of
+    forces that let runs at different GPU counts be compared atom by atom."""
+    import torch
+    case = Case(ljx, "c4", "float64", world, rank, local)
+    timing = case.time(args.steps, args.warmup, 10)
+    total = case.total_atoms()
+    sample_ids = np.linspace(0, total - 1, C4_SAMPLES).astype(np.int64)
+    energy, virial, fmax, forces = case.clean_forces(sample_ids, 10)
+    elapsed = timing["elapsed"]
+    out = {
+        "workload": CONFIGS["c4"]["title"].format(c=CONFIGS["c4"]["cells"]),
+        "total_atoms": total, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "value": total * args.steps / elapsed,
+        "unit": UNIT, "scaling": "strong", "gpu_launches": timing["launches"],
+        "phase_ms": {n: v * 1e3 for n, v in timing["phase"].items()},
+        "parallelism": case.decomp["parallelism"],
+        "energy": energy, "virial": virial, "max_abs_force": fmax,
+        "force_sample": {"ids": [int(i) for i in sample_ids],
+                         "f": [forces.get(int(i)) for i in sample_ids]},
+        "system": "one crystal at every GPU count: each unit-cell z-layer draws its jitter and "
+                  "species from its own seed (synth.fcc_layers), so energy, virial and the "
+                  "sampled forces compare across runs",
+    }
+    case.close()
+    del case
+    torch.cuda.empty_cache()
+    return out
 
 
 def _bundle(ljx, cfg, path, max_atoms, precision):
@@ -425,22 +525,23 @@ def liquid_atoms(ljx, cfg, cells):
     4 * cells^3 atoms when cells is not a multiple of 20)."""
     tiles, edge = (cells // 20, 20) if cells % 20 == 0 else (1, cells)
     n_tile = 4 * edge ** 3
-    types = _types_fn(cfg)(n_tile, 2025)
+    types = ljx.synth.substitutional(n_tile, cfg["fractions"], seed=2025)
     return ljx.synth.liquid_packing(n_tile, cfg["liquid"], 2.0, seed=2024, tiles=tiles,
                                     types=types)
+
+
+def crystal_atoms(ljx, cfg, cells):
+    """The C3 / C4 crystal of `cells` unit cells: fcc_layers, wrapped and sorted as LAMMPS does
+    (the same atoms as every slab decomposition of it)."""
+    return ljx.synth.layered_crystal(cells, cfg["lattice"], JITTER, 2024, cfg["fractions"])
 
 
 def setup_single(ljx, cfg, cells, precision):
     import tempfile
 
     import torch
-    types_fn = _types_fn(cfg)
-    if cfg.get("liquid"):
-        atoms = liquid_atoms(ljx, cfg, cells[0])
-    else:
-        n = 4 * cells[0] * cells[1] * cells[2]
-        types = types_fn(n, 2025) if types_fn else None
-        atoms = ljx.synth.fcc(cells, cfg["lattice"], jitter=JITTER, seed=2024, types=types)
+    atoms = (liquid_atoms(ljx, cfg, cells[0]) if cfg.get("liquid")
+             else crystal_atoms(ljx, cfg, cells))
     x_all, owner = ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)
     types_all = np.concatenate([atoms.types, atoms.types[owner]]).astype(np.int32)
     nlocal, nall = len(atoms.x), len(x_all)
@@ -460,19 +561,26 @@ def setup_single(ljx, cfg, cells, precision):
     # Ghost rows as images of owned rows: whole box lengths per dimension (LAMMPS's pbc shift).
     shift = np.round((x_all[nlocal:] - x_all[owner]) / atoms.box) * atoms.box
     ghosts = (system.comm.owner, torch.as_tensor(shift, device="cuda"))
-    return system, nlocal, nall, {"pair": pair, "parallelism": "single GPU (periodic self-images)",
-                                  "comm_launches": 1, "lists": builder, "ghosts": ghosts}
+    ids = atoms.ids if atoms.ids is not None else np.arange(nlocal)
+    exchanges = "reverse rho, forward F'(rho) and reverse forces" if cfg["newton"] else "F'(rho)"
+    # SelfComm's kernels (one per exchange) are libljx's but not counted by the engine.
+    return system, nlocal, nall, {"pair": pair,
+                                  "parallelism": "single GPU (periodic self-images; "
+                                                 f"{exchanges} by ljx_halo_*_self)",
+                                  "extra_launches": 3 if cfg["newton"] else 1,
+                                  "lists": builder, "ghosts": ghosts, "ids": ids}
 
 
 def setup_decomposed(ljx, cfg, cells, rank, world, precision, local):
-    """Rank `rank` of a z-slab decomposition of `cells` per rank."""
+    """Rank `rank` of a z-slab decomposition of `cells` per rank, exchanging over libljx's NCCL
+    halo (ljx_halo)."""
     import tempfile
 
     import torch
     from importlib import import_module
     halo = import_module("lammps_jax_b200.halo")
     slab = ljx.synth.slab_decomposition(cells, cfg["lattice"], JITTER, 2024, rank, world,
-                                        CUTOFF + SKIN, types_fn=_types_fn(cfg))
+                                        CUTOFF + SKIN, fractions=cfg["fractions"])
     nlocal, nall = slab.nlocal, len(slab.x)
     path = Path(tempfile.mkdtemp()) / f"bench_rank{rank}.json"
     _bundle(ljx, cfg, path, nall + 1024, precision)
@@ -486,14 +594,15 @@ def setup_decomposed(ljx, cfg, cells, rank, world, precision, local):
     pair.init_style(system)
     builder = ljx.synth.DeviceListBuilder(slab.x, nlocal, CUTOFF + SKIN, half=cfg["half"])
     system.list = builder.build(x)
-    elem = 8 if precision == "float64" else 4
-    system.comm = halo.SlabExchange(slab, 1, elem)
+    nccl = halo.NcclHalo(halo.slab_swaps(slab, rank, world), rank, world, local, timeout_ms=60000)
+    system.comm = nccl
     exchanges = "reverse rho, forward F'(rho) and reverse forces" if cfg["newton"] else "F'(rho)"
     return system, nlocal, nall, {
-        "pair": pair, "comm_launches": system.comm.launches_per_exchange, "lists": builder,
-        "parallelism": f"z-slab spatial decomposition over {world} GPUs; {exchanges} by grouped "
-                       "NCCL send/recv with both z-neighbors + x/y periodic images",
-        "close": lambda: None}
+        "pair": pair, "extra_launches": 0, "lists": builder, "halo": nccl, "ids": slab.ids,
+        "parallelism": f"z-slab spatial decomposition over {world} GPUs; {exchanges} by libljx's "
+                       "NCCL halo (ljx_halo: gather kernel, grouped ncclSend/ncclRecv with both "
+                       "z-neighbors, x/y periodic images on the device); step totals by one "
+                       "on-stream NCCL all-reduce (ljx_read_result_all)"}
 
 
 def run_md(torch, ljx, cfg, cells, precision, steps, warmup):
@@ -554,13 +663,14 @@ def time_list_build(torch, lists, x, stream, reps=5):
     return start.elapsed_time(stop) / reps
 
 
-def run_e2e(torch, system, core, args, world, lists, total_atoms, ghosts=None):
+def run_e2e(torch, case, args, world, total_atoms):
     """Same step through the C ABI with host buffers: H2D of x and D2H of the forces and the
     result every step. Every `rebuild_every`-th step (10 for C3 and C4, every step for C5) the
     neighbor list is rebuilt on the device from the uploaded positions (ljx_neigh_bin +
     ljx_neigh_build into the same buffers), as LAMMPS-Kokkos builds it on the device."""
     import ctypes
 
+    system, lists, ghosts = case.system, case.decomp["lists"], case.decomp.get("ghosts")
     period = args.rebuild_every if args.rebuild_every > 0 else 10
     nlocal, nghost = system.nlocal, system.nghost
     # One rank owning the whole box: upload the owned positions and fill their periodic images on
@@ -570,7 +680,7 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms, ghosts=None):
     owned_only = ghosts is not None
     x_host = (system.x[:nlocal] if owned_only else system.x).cpu().pin_memory()
     f_host = torch.empty_like(system.f[:nlocal], device="cpu").pin_memory()
-    stream = torch.cuda.current_stream()
+    stream = case.stream
     steps = max(3, min(args.steps, 10))
     lib = package().abi.load()
 
@@ -588,9 +698,9 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms, ghosts=None):
             system.x.copy_(x_host, non_blocking=True)
         if k % period == 0:
             lists.launch(system.x, stream)
-        core(k % period if args.rebuild_every > 0 else -1)  # ends with the result read (a sync)
+        case.core(k % period if args.rebuild_every > 0 else -1)  # ends with the result read
         f_host.copy_(system.f[:nlocal], non_blocking=True)
-        torch.cuda.current_stream().synchronize()        # forces on the host
+        stream.synchronize()                                    # forces on the host
         return x_host.numel() * 8
 
     one(1)
@@ -610,7 +720,8 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms, ghosts=None):
         elapsed = float(t.item())
     value = total_atoms * steps / elapsed
     return {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d / steps,
-            "d2h_bytes_per_step": f_host.numel() * 8 + 9 * 8, "steps": steps,
+            "d2h_bytes_per_step": f_host.numel() * 8 + (12 if world > 1 else 9) * 8,
+            "steps": steps,
             "x_upload": ("owned rows; periodic images filled on the device (ljx_ghost_positions)"
                          if owned_only else "owned and ghost rows"),
             "list": ("rebuilt on the device every step from the uploaded positions" if period == 1
@@ -619,53 +730,64 @@ def run_e2e(torch, system, core, args, world, lists, total_atoms, ghosts=None):
 
 
 def reference_sample(ljx, oracle, args):
-    """A bounded CPU sample of the bench workload for the oracle: a 40^3-cell replica of the C3 or
-    C4 crystal (the same lattice, species, potential, cutoffs and list kind) or one 32,000-atom
-    tile of the C5 liquid. Returns (one_step, atoms, description)."""
+    """The bench workload for the CPU oracle (the restatement of the reference's path): the
+    C3 crystal of one GPU's share (2,048,000 atoms, the same atoms as the N=1 GPU run), the full
+    C5 liquid, or for C4 (16.4 M atoms, minutes per CPU step) a 40^3-cell replica of its crystal.
+    Returns (one_step, atoms, workload text, same_config)."""
     cfg = CONFIGS[args.config]
+    cells = args.cells or cfg["cells"]
     if cfg.get("liquid"):
-        atoms = liquid_atoms(ljx, cfg, 20)
-        what = "one 32,000-atom tile of the C5 liquid"
+        atoms = liquid_atoms(ljx, cfg, cells)
+        same = True
+    elif cfg["strong"]:
+        atoms = crystal_atoms(ljx, cfg, (40, 40, 40))
+        same = False
     else:
-        n = 40
-        tf = _types_fn(cfg)
-        atoms = ljx.synth.fcc((n, n, n), cfg["lattice"], jitter=JITTER, seed=7,
-                              types=tf(4 * n ** 3, 2025) if tf else None)
-        what = f"{n}^3-cell replica of the {args.config.upper()} crystal"
+        atoms = crystal_atoms(ljx, cfg, (cells, cells, cells))
+        same = True
     x_all, owner = ljx.synth.periodic_ghosts(atoms.x, atoms.box, CUTOFF + SKIN)
     types_all = np.concatenate([atoms.types, atoms.types[owner]]).astype(np.int32)
     nlocal = len(atoms.x)
     tables = oracle.parse_setfl_text(ljx.synth.synthetic_setfl(cfg["elements"]))
     lst = oracle.build_list(x_all, nlocal, CUTOFF + SKIN, half=cfg["half"])
     mode = "half-unique" if cfg["half"] else "rows-full"
+    workload = cfg["title"].format(c=cells if same else 40) + f" ({nlocal:,} atoms in all)"
 
     def one_step():
         oracle.eam_step(tables, x_all, types_all, nlocal, owner, lst, mode=mode,
                         precision=args.precision)
 
-    return one_step, nlocal, f"{what} ({nlocal} atoms, {mode}, {args.precision})"
+    return one_step, nlocal, workload, same
+
+
+CPU_STEP_BUDGET_S = 420.0
 
 
 def cpu_baseline(args, steps=2):
-    """The CPU restatement (oracle, all host threads) on a bounded replica of the workload."""
+    """The CPU restatement (oracle, all host threads) on the workload of one GPU, a bounded
+    number of steps."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
     oracle.lib()
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
-    one_step, nlocal, what = reference_sample(package(), oracle, args)
-    one_step()
+    one_step, nlocal, workload, _ = reference_sample(package(), oracle, args)
     t0 = time.perf_counter()
     for _ in range(steps):
         one_step()
     dt = time.perf_counter() - t0
     return {"value": nlocal * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{what}: {steps} full steps (pack + density + embedding + exchange + "
-                      "forces + virial), oracle/eam_oracle.c with OpenMP"}
+            "sample": f"{workload}: {steps} full steps (pack from the list + density + "
+                      "embedding + exchange + forces + virial), oracle/eam_oracle.c with "
+                      f"OpenMP on {threads} threads"}
 
 
 def run_reference(args):
+    """The reference's path on the host cores: the CPU restatement of its per-step work
+    (oracle/, OpenMP on every host thread) on the bench's own workload, `warmup` untimed and
+    `steps` timed steps. Under torchrun only rank 0 runs it; the others exit without work."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -674,29 +796,38 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
     cfg = CONFIGS[args.config]
-    one_step, nlocal, what = reference_sample(package(), oracle, args)
-    steps = max(1, min(args.steps, 5))
-    for _ in range(min(args.warmup, 1)):
+    one_step, nlocal, workload, same = reference_sample(package(), oracle, args)
+    t0 = time.perf_counter()
+    for _ in range(args.warmup):
         one_step()
+    per_step = (time.perf_counter() - t0) / max(1, args.warmup)
+    # All the requested steps when they fit the budget (the driver's runs do); otherwise as many
+    # as fit, said in the line.
+    steps = (args.steps if args.warmup == 0 or per_step * args.steps <= CPU_STEP_BUDGET_S
+             else max(1, int(CPU_STEP_BUDGET_S / per_step)))
     t0 = time.perf_counter()
     for _ in range(steps):
         one_step()
     dt = time.perf_counter() - t0
     value = nlocal * steps / dt
-    sample = f"{what}, {steps} timed steps"
+    share = "" if world == 1 else (f"; the GPU run's {world} ranks each own a share of this size "
+                                   "(weak scaling), the CPU runs one share")
+    sample = (f"{workload}, {args.warmup} warm-up and {steps} timed steps on {threads} threads"
+              + ("" if same else "; a 40^3-cell replica of the C4 crystal") + share)
     print(json.dumps({
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
-        "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": dt / steps * 1e3,
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": dt / steps * 1e3,
         "higher_is_better": True, "scaling": cfg["scaling"], "vs_baseline": None,
         "dtype": "f64" if args.precision == "float64" else "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": cfg["title"].format(c=cfg["cells"]) + " (CPU sample)",
-                   "name": args.config, "precision": args.precision},
+        "config": {"workload": workload, "name": args.config, "total_atoms": nlocal,
+                   "precision": args.precision},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference's own CPU path (LAMMPS Kokkos-OpenMP + XLA CPU PJRT) is not "
-                "installable offline; this times the CPU restatement of that path",
+        "note": "the reference's own CPU path (LAMMPS Kokkos-OpenMP + XLA CPU PJRT) cannot be "
+                "installed offline (no LAMMPS, MPI, jaxlib or PJRT plugin on the box); this "
+                "times oracle/eam_oracle.c, the CPU restatement of that path's per-step work",
     }), flush=True)
 
 
@@ -720,11 +851,13 @@ def main():
                          "2,048,000-atom config), of the whole box for c4 (default 160); the "
                          "fcc-cell equivalent of the liquid box for c5 (default 80)")
     ap.add_argument("--skip-extras", action="store_true",
-                    help="time the device path only (no e2e or CPU-baseline legs); for profiling")
+                    help="time the device path only (no e2e, MD, C4 or CPU-baseline legs); for "
+                         "profiling")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="leave out the C4 strong-scaling object of the c3 line")
     args = ap.parse_args()
     if args.precision is None:
         args.precision = CONFIGS[args.config].get("precision", "float64")
-    (ROOT / "gpurun_out").mkdir(exist_ok=True)
     if args.impl == "reference":
         run_reference(args)
     else:
