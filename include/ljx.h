@@ -204,6 +204,19 @@ ljx_status ljx_force(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
 ljx_status ljx_energy(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
                       const ljx_list *list, int newton_pair, double scale);
 
+/* Per-atom energy and virial: LAMMPS's eatom / vatom under eflag_atom / vflag_atom, which the
+ * reference refuses (cpp/pair_jax_kokkos.cpp:995-996). eatom is double[nall], vatom
+ * double[nall][6] (xx, yy, zz, xy, xz, yz), device memory on the engine's device; either may be
+ * NULL. The ljx_embed, ljx_force and ljx_energy calls that follow ADD into them (LAMMPS's
+ * ev_setup zeroes them first), times `scale` (the pair_coeff scale), until the next call here
+ * (NULL, NULL turns the tallies off). The split is LAMMPS's ev_tally: the embedding energy
+ * F(rho_i) goes to atom i; half of each pair's energy and half of its virial -rij (x) F go to each
+ * of the two atoms (a full-list row takes its own half, the pair's other row the other).
+ * Newton-on modes also write ghost rows, which LAMMPS's compute pe/atom and stress/atom fold into
+ * their owners by reverse comm. Without these arrays the force pass runs without the tally work.
+ */
+ljx_status ljx_set_atom_tallies(ljx_engine *engine, double *eatom, double *vatom, double scale);
+
 /* Reduces the step's energy/virial/counters and copies them to the host (one stream sync). */
 ljx_status ljx_read_result(ljx_engine *engine, void *stream, ljx_result *out);
 

@@ -73,6 +73,14 @@ ljx_status ljx_pair_compute(ljx_pair *pair, void *stream, const ljx_atoms *atoms
                             const ljx_list *list, int newton_pair, int flags,
                             const ljx_pair_host *host, ljx_result *out);
 
+/* LAMMPS's per-atom arrays for eflag_atom / vflag_atom computes: Pair::eatom double[nmax] and
+ * Pair::vatom double[nmax][6] (the Kokkos pair's d_eatom / d_vatom), device memory; either may
+ * be NULL. With an array registered, compute accepts the matching flag instead of the
+ * reference's refusal (cpp/pair_jax_kokkos.cpp:995-996): it zeroes nlocal (+ nghost with newton
+ * on) rows as ev_setup does and fills them as LAMMPS's ev_tally splits pair terms (see
+ * ljx_set_atom_tallies). The plugin re-registers them when LAMMPS grows the arrays. */
+ljx_status ljx_pair_set_atom_tallies(ljx_pair *pair, double *eatom, double *vatom);
+
 /* Pair::eng_vdwl and Pair::virial[6] after the last compute (reset by its flags, as ev_init). */
 ljx_status ljx_pair_tally(const ljx_pair *pair, double *eng_vdwl, double *virial);
 

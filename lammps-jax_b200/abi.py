@@ -128,6 +128,7 @@ SIGNATURES = [
     ("ljx_lj_force_noalloc", c_int, [c_void_p, POINTER(Atoms), POINTER(NeighList), c_double,
                                      c_double, c_double, c_int, c_int, c_int, c_double,
                                      c_void_p]),
+    ("ljx_set_atom_tallies", c_int, [c_void_p, c_void_p, c_void_p, c_double]),
     ("ljx_engine_launches", c_longlong, [c_void_p]),
     ("ljx_pair_create", c_int, [c_int, POINTER(c_void_p)]),
     ("ljx_pair_destroy", None, [c_void_p]),
@@ -140,6 +141,7 @@ SIGNATURES = [
     ("ljx_pair_compute", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
                                  c_int, POINTER(PairHost), POINTER(Result)]),
     ("ljx_pair_tally", c_int, [c_void_p, POINTER(c_double), POINTER(c_double)]),
+    ("ljx_pair_set_atom_tallies", c_int, [c_void_p, c_void_p, c_void_p]),
     ("ljx_pair_bundle", c_void_p, [c_void_p]),
     ("ljx_pair_engine", c_void_p, [c_void_p]),
     ("ljx_version", c_char_p, []),

@@ -126,6 +126,10 @@ struct ljx_engine {
   int last_nall = 0;
   double last_scale = 1.0;
   int last_duplicate = 1;
+  // Per-atom tallies (ljx_set_atom_tallies): caller-owned device arrays, null when off.
+  double *eatom = nullptr;
+  double *vatom = nullptr;
+  double tally_scale = 1.0;
   long long launches = 0;
   std::string error;
 
@@ -314,6 +318,9 @@ ljx::Step<T> make_step(ljx_engine *e, const ljx_atoms *a, const ljx_list *l, dou
   p.lj_four_eps = static_cast<T>(4.0 * e->c.lj_epsilon);
   p.lj_sigma_sq = static_cast<T>(e->c.lj_sigma * e->c.lj_sigma);
   p.lj_energy_scale = static_cast<T>(e->c.lj_edge_energy_scale);
+  p.eatom = e->eatom;
+  p.vatom = e->vatom;
+  p.tally_scale = e->tally_scale;
   return p;
 }
 
@@ -440,23 +447,22 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   e->step_blocks[kDensityPart] = grid;
 }
 
-template <typename T, bool FORCES = true>
-void launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+template <typename T, bool FORCES, bool TALLY>
+void launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
 {
-  if (p.inum <= 0) return;
   int grid = 0;
   switch (mode) {
     case ljx::kGhost:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kGhost, FORCES>));
-      ljx::k_force<T, ljx::kGhost, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kGhost, FORCES, TALLY>));
+      ljx::k_force<T, ljx::kGhost, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     case ljx::kHalf:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kHalf, FORCES>));
-      ljx::k_force<T, ljx::kHalf, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kHalf, FORCES, TALLY>));
+      ljx::k_force<T, ljx::kHalf, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     default:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kRowsFull, FORCES>));
-      ljx::k_force<T, ljx::kRowsFull, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY>));
+      ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
   }
   check_launch("k_force");
   e->launches++;
@@ -464,30 +470,51 @@ void launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode
 }
 
 template <typename T, bool FORCES = true>
-void launch_lj(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+void launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
 {
   if (p.inum <= 0) return;
+  // The per-atom tally variants run only when a caller asked for per-atom output.
+  if (p.eatom != nullptr || p.vatom != nullptr)
+    launch_force_as<T, FORCES, true>(e, s, p, mode);
+  else
+    launch_force_as<T, FORCES, false>(e, s, p, mode);
+}
+
+template <typename T, bool FORCES, bool TALLY>
+void launch_lj_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+{
   int grid = 0;
   switch (mode) {
     case ljx::kLjEdgeHalf:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeHalf, FORCES>));
-      ljx::k_lj<T, ljx::kLjEdgeHalf, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeHalf, FORCES, TALLY>));
+      ljx::k_lj<T, ljx::kLjEdgeHalf, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     case ljx::kLjAtomFull:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomFull, FORCES>));
-      ljx::k_lj<T, ljx::kLjAtomFull, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomFull, FORCES, TALLY>));
+      ljx::k_lj<T, ljx::kLjAtomFull, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     case ljx::kLjAtomHalfPairSum:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomHalfPairSum, FORCES>));
-      ljx::k_lj<T, ljx::kLjAtomHalfPairSum, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum,
+                      blocks_per_sm(ljx::k_lj<T, ljx::kLjAtomHalfPairSum, FORCES, TALLY>));
+      ljx::k_lj<T, ljx::kLjAtomHalfPairSum, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
     default:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeFull, FORCES>));
-      ljx::k_lj<T, ljx::kLjEdgeFull, FORCES><<<grid, ljx::kBlock, 0, s>>>(p);
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_lj<T, ljx::kLjEdgeFull, FORCES, TALLY>));
+      ljx::k_lj<T, ljx::kLjEdgeFull, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
   }
   check_launch("k_lj");
   e->launches++;
   e->step_blocks[kLjPart] = grid;
+}
+
+template <typename T, bool FORCES = true>
+void launch_lj(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+{
+  if (p.inum <= 0) return;
+  if (p.eatom != nullptr || p.vatom != nullptr)
+    launch_lj_as<T, FORCES, true>(e, s, p, mode);
+  else
+    launch_lj_as<T, FORCES, false>(e, s, p, mode);
 }
 
 template <typename T>
@@ -1034,6 +1061,15 @@ ljx_status ljx_feature_rows(ljx_engine *e, int which, void **rows, int *width, i
   *rows = which == 0 ? e->rho : e->fp;
   if (width) *width = 1;
   if (elem_bytes) *elem_bytes = e->f64 ? 8 : 4;
+  return LJX_OK;
+}
+
+ljx_status ljx_set_atom_tallies(ljx_engine *e, double *eatom, double *vatom, double scale)
+{
+  if (e == nullptr) return LJX_ERR_INVALID;
+  e->eatom = eatom;
+  e->vatom = vatom;
+  e->tally_scale = scale;
   return LJX_OK;
 }
 

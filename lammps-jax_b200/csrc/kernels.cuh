@@ -38,8 +38,9 @@ constexpr int kQueue = 64;
 #endif
 // The force pass: 4 blocks of 256 per SM (64 registers); the double half-list variant, which
 // spills at 64, runs 3 (80 registers) and is faster for it.
-#define LJX_FORCE_BOUNDS \
-  __launch_bounds__(kBlock, (sizeof(T) == 8 && MODE == kHalf) ? 3 : LJX_FORCE_MIN_BLOCKS)
+#define LJX_FORCE_BOUNDS                                                                   \
+  __launch_bounds__(kBlock, TALLY ? 2                                                       \
+                            : (sizeof(T) == 8 && MODE == kHalf) ? 3 : LJX_FORCE_MIN_BLOCKS)
 
 enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2 };
 // Force distribution modes.
@@ -129,6 +130,11 @@ struct Step {
   int rcap;
   // Per-block partial sums.
   double *partials;
+  // Per-atom tallies (LAMMPS eatom[nall], vatom[nall][6]; null when not asked for), accumulated
+  // with += times tally_scale.
+  double *eatom;
+  double *vatom;
+  double tally_scale;
 };
 
 __device__ __forceinline__ double warp_sum(double v)
@@ -531,6 +537,8 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
     if (t_raw > t) sl = end;
     p.fp[i] = sl * inv_drho;
     e += static_cast<double>(v);
+    // Per-atom energy: the embedding term belongs to atom i alone.
+    if (p.eatom != nullptr) p.eatom[i] += p.tally_scale * static_cast<double>(v);
   }
   double acc[8] = {e, 0, 0, 0, 0, 0, 0, 0};
   store_partials(acc, 0, p.partials);
@@ -542,10 +550,16 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
 // comes from the pre-scaled slope table. Accumulates the row force and the thread's pair energy
 // and virial (both without their constant weights, applied once per block). Without FORCES only
 // the pair energy is accumulated (energy-only evaluation).
-template <typename T, int MODE, bool FORCES = true>
+//
+// TALLY adds the per-atom split of LAMMPS's ev_tally: atom i always takes half the pair energy
+// phi and half of this edge's -rij (x) F_e into the row sums er / vr; the neighbor j takes the
+// other half of the energy when each pair appears once (half list) and the other half of the
+// virial when the force acts on j too (newton-on scatter), both by atomics into its rows.
+template <typename T, int MODE, bool FORCES = true, bool TALLY = false>
 __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T>::type &pi,
                                          int si, T fpi, int j, const typename Vec4<T>::type &pj,
-                                         T fpj, T &fx, T &fy, T &fz, double &e, double (&v)[6])
+                                         T fpj, T &fx, T &fy, T &fz, double &e, double (&v)[6],
+                                         double &er, double (&vr)[6])
 {
   const T dx = pj.x - pi.x, dy = pj.y - pi.y, dz = pj.z - pi.z;
   const T r2 = dx * dx + dy * dy + dz * dz;
@@ -561,6 +575,11 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   const T z2 = c.x + t * (c.y + t * (c.z + t * c.w));
   const T phi = z2 * rinv;
   e += static_cast<double>(phi);
+  if constexpr (TALLY) {
+    er += 0.5 * static_cast<double>(phi);
+    if (MODE == kHalf && p.eatom != nullptr && j < p.nall)
+      atomicAdd(p.eatom + j, p.tally_scale * 0.5 * static_cast<double>(phi));
+  }
   if constexpr (FORCES) {
     const auto dj = load4(p.density_slope + sj * p.nr + node);
     const T rhojp = dj.x + t * (dj.y + t * dj.z);
@@ -580,16 +599,49 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
     fx += ex;
     fy += ey;
     fz += ez;
-    v[0] += static_cast<double>(dx * ex);
-    v[1] += static_cast<double>(dy * ey);
-    v[2] += static_cast<double>(dz * ez);
-    v[3] += static_cast<double>(dx * ey);
-    v[4] += static_cast<double>(dx * ez);
-    v[5] += static_cast<double>(dy * ez);
+    const double c6[6] = {static_cast<double>(dx * ex), static_cast<double>(dy * ey),
+                          static_cast<double>(dz * ez), static_cast<double>(dx * ey),
+                          static_cast<double>(dx * ez), static_cast<double>(dy * ez)};
+#pragma unroll
+    for (int k = 0; k < 6; ++k) v[k] += c6[k];
+    if constexpr (TALLY) {
+#pragma unroll
+      for (int k = 0; k < 6; ++k) vr[k] -= 0.5 * c6[k];
+      if (MODE != kRowsFull && p.vatom != nullptr && j < p.nall)
+#pragma unroll
+        for (int k = 0; k < 6; ++k) atomicAdd(p.vatom + 6 * j + k, -0.5 * p.tally_scale * c6[k]);
+    }
     if (MODE != kRowsFull && j < p.nall) {
       atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
       atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
       atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
+    }
+  }
+}
+
+// Adds a row's per-atom sums (TALLY) into eatom[i] / vatom[i]: plain adds when no other row
+// scatters into atom i (PLAIN: full list without newton-on scatters), atomics otherwise.
+template <typename T, bool PLAIN>
+__device__ __forceinline__ void tally_row(const Step<T> &p, int lane, int i, double er,
+                                          double (&vr)[6])
+{
+  er = warp_sum(er);
+#pragma unroll
+  for (int k = 0; k < 6; ++k) vr[k] = warp_sum(vr[k]);
+  if (lane != 0 || i >= p.nall) return;
+  if (p.eatom != nullptr) {
+    if (PLAIN)
+      p.eatom[i] += p.tally_scale * er;
+    else
+      atomicAdd(p.eatom + i, p.tally_scale * er);
+  }
+  if (p.vatom != nullptr) {
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+      if (PLAIN)
+        p.vatom[6 * i + k] += p.tally_scale * vr[k];
+      else
+        atomicAdd(p.vatom + 6 * i + k, p.tally_scale * vr[k]);
     }
   }
 }
@@ -607,13 +659,15 @@ __device__ __forceinline__ typename Vec4<T>::type load_pos(const Step<T> &p, int
 // a9..a13: fused force + pair energy + virial over the compacted rows. Spilled rows (more kept
 // pairs than row_cap) re-walk the LAMMPS list with the same filter. Without FORCES: the pair
 // energy alone (energy-only evaluation; no F', no force or virial).
-template <typename T, int MODE, bool FORCES = true>
+template <typename T, int MODE, bool FORCES = true, bool TALLY = false>
 __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
 {
   using V = typename Vec4<T>::type;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double e = 0.0;
   double v[6] = {0, 0, 0, 0, 0, 0};
+  double er = 0.0;                      // per-atom tallies of the current row (TALLY)
+  double vr[6] = {0, 0, 0, 0, 0, 0};
   constexpr bool kNeedFpj = FORCES && MODE != kGhost;
   // Float runs and the half-list mode (80 registers) load the next row's atom and kept count
   // one row ahead, so a row's dependent loads (atom -> position and F') start without waiting
@@ -644,14 +698,20 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
     const int si = static_cast<int>(pi.w);
     const T fpi = FORCES ? p.fp[i] : T(0);
     T fx = T(0), fy = T(0), fz = T(0);
+    if constexpr (TALLY) {
+      er = 0.0;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) vr[k] = 0.0;
+    }
     if (n <= p.row_cap) {
       const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
       if constexpr (sizeof(T) == 8) {
         // (Pipelining as below spills at 64 registers in double runs and loses.)
         for (int k = lane; k < n; k += kWarp) {
           const int j = crow[k];
-          eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, load_pos(p, j),
-                                    kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
+          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, load_pos(p, j),
+                                           kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
+                                           er, vr);
         }
       } else {
         // Float runs are software-pipelined by one pair: the next pair's position and F' gathers
@@ -676,7 +736,8 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
             pj2 = load_pos(p, j2);
             if (kNeedFpj) fpj2 = __ldg(p.fp + j2);
           }
-          eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v);
+          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v, er,
+                                           vr);
           k = k2;
           j = j2;
           pj = pj2;
@@ -691,8 +752,9 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
         const int j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
         if (j >= p.max_atoms) continue;
         if (pack_keep(p, i, xi, j, load4(p.xd4 + j)))
-          eam_edge<T, MODE, FORCES>(p, pi, si, fpi, j, load_pos(p, j),
-                                    kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v);
+          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, load_pos(p, j),
+                                           kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
+                                           er, vr);
       }
     }
     if constexpr (FORCES) {
@@ -712,6 +774,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
         }
       }
     }
+    if constexpr (TALLY) tally_row<T, MODE == kRowsFull>(p, lane, i, er, vr);
   }
   // Pair energy: phi/2 per directed edge of a full list, phi per edge of a half list. Virial:
   // -1/2 rij (x) F_e when every pair appears in two rows, -rij (x) F_e when the receiver takes
@@ -724,7 +787,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
 
 // LJ 12-6 in one pass over the LAMMPS list: examples/export_model.py:16-74 with the force-add
 // conventions of cpp/pair_jax_kokkos.cpp:176-225. Without FORCES: the energy alone.
-template <typename T, int MODE, bool FORCES = true>
+template <typename T, int MODE, bool FORCES = true, bool TALLY = false>
 __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
 {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -732,6 +795,11 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
   double v[6] = {0, 0, 0, 0, 0, 0};
   int widest = 0;
   const bool scatter = MODE != kLjEdgeFull;
+  // Per-atom split (TALLY): a half list holds each pair once, so its energy goes half to each
+  // atom; a scattering mode applies the force to both atoms, so its virial goes half to each.
+  constexpr bool kHalfList = MODE == kLjEdgeHalf || MODE == kLjAtomHalfPairSum;
+  double er = 0.0;
+  double vr[6] = {0, 0, 0, 0, 0, 0};
   // Sender weight (edge-force bundles add dU/drij; atom-force bundles the energy-scaled
   // gradient, doubled for pair-sum half lists that stand for both directions).
   const T fw = MODE == kLjAtomFull ? p.lj_energy_scale
@@ -750,6 +818,11 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
     const long long rowbase = static_cast<long long>(i) * p.atom_stride;
     T fx = T(0), fy = T(0), fz = T(0);
     int kept = 0;
+    if constexpr (TALLY) {
+      er = 0.0;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) vr[k] = 0.0;
+    }
     for (int base = 0; base < n; base += kWarp) {
       const int jj = base + lane;
       bool keep = false;
@@ -770,7 +843,13 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
       const T inv_r2 = p.lj_sigma_sq / r2;
       const T inv_r6 = inv_r2 * inv_r2 * inv_r2;
       const T u = p.lj_four_eps * (inv_r6 * inv_r6 - inv_r6);
-      e += static_cast<double>(ew * u);
+      const double eu = static_cast<double>(ew * u);
+      e += eu;
+      if constexpr (TALLY) {
+        er += kHalfList ? 0.5 * eu : eu;
+        if (kHalfList && p.eatom != nullptr && j < p.nall)
+          atomicAdd(p.eatom + j, p.tally_scale * 0.5 * eu);
+      }
       if constexpr (!FORCES) continue;
       // dU/drij = 2 rij dU/d(r^2), dU/d(r^2) = -4 eps (6 a^6 - 3 a^3) / r^2, a = sigma^2/r^2.
       const T g = T(-2) * p.lj_four_eps * (T(6) * inv_r6 * inv_r6 - T(3) * inv_r6) / r2 * fw;
@@ -778,12 +857,20 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
       fx += ex;
       fy += ey;
       fz += ez;
-      v[0] -= vw * static_cast<double>(dx * ex);
-      v[1] -= vw * static_cast<double>(dy * ey);
-      v[2] -= vw * static_cast<double>(dz * ez);
-      v[3] -= vw * static_cast<double>(dx * ey);
-      v[4] -= vw * static_cast<double>(dx * ez);
-      v[5] -= vw * static_cast<double>(dy * ez);
+      const double c6[6] = {static_cast<double>(dx * ex), static_cast<double>(dy * ey),
+                            static_cast<double>(dz * ez), static_cast<double>(dx * ey),
+                            static_cast<double>(dx * ez), static_cast<double>(dy * ez)};
+#pragma unroll
+      for (int k = 0; k < 6; ++k) v[k] -= vw * c6[k];
+      if constexpr (TALLY) {
+        const double wi = scatter ? 0.5 * vw : vw;
+#pragma unroll
+        for (int k = 0; k < 6; ++k) vr[k] -= wi * c6[k];
+        if (scatter && p.vatom != nullptr && j < p.nall)
+#pragma unroll
+          for (int k = 0; k < 6; ++k)
+            atomicAdd(p.vatom + 6 * j + k, -0.5 * vw * p.tally_scale * c6[k]);
+      }
       if (scatter && j < p.nall) {
         atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
         atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
@@ -807,6 +894,7 @@ __global__ void __launch_bounds__(kBlock) k_lj(const Step<T> p)
         }
       }
     }
+    if constexpr (TALLY) tally_row<T, MODE == kLjEdgeFull>(p, lane, i, er, vr);
     kept_sum += kept;
   }
   double acc[8] = {e, v[0], v[1], v[2], v[3], v[4], v[5], lane == 0 ? kept_sum : 0.0};

@@ -4,6 +4,8 @@
 
 #include "ljx_pair.h"
 
+#include <cuda_runtime.h>
+
 #include <cerrno>
 #include <cmath>
 #include <cstdlib>
@@ -80,6 +82,8 @@ struct ljx_pair {
   bool planned = false;
   double eng_vdwl = 0.0;
   double virial[6] = {0, 0, 0, 0, 0, 0};
+  double *eatom = nullptr;  // LAMMPS's per-atom arrays (device), registered by the plugin
+  double *vatom = nullptr;
   std::string error;
 
   ljx_status fail(ljx_status status, std::string message)
@@ -222,9 +226,10 @@ ljx_status ljx_pair_compute(ljx_pair *pair, void *stream, const ljx_atoms *atoms
     for (double &v : pair->virial) v = 0.0;
   if (!pair->model_loaded || pair->engine == nullptr)
     return pair->fail(LJX_ERR_INVALID, "LAMMPS-JAX runtime is not initialized");
-  if (flags & LJX_EFLAG_ATOM)
+  // Per-atom output needs LAMMPS's arrays; without them the reference's refusal stands.
+  if ((flags & LJX_EFLAG_ATOM) && pair->eatom == nullptr)
     return pair->fail(LJX_ERR_UNSUPPORTED, "pair jax/kk does not support per-atom energy output");
-  if (flags & LJX_VFLAG_ATOM)
+  if ((flags & LJX_VFLAG_ATOM) && pair->vatom == nullptr)
     return pair->fail(LJX_ERR_UNSUPPORTED, "pair jax/kk does not support per-atom virial output");
   // Energy-only (MC) steps need an energy program in the reference; a bundle's potential block
   // always yields the energy here.
@@ -257,6 +262,21 @@ ljx_status ljx_pair_compute(ljx_pair *pair, void *stream, const ljx_atoms *atoms
     return pair->fail(LJX_ERR_CAPACITY, "LAMMPS-JAX owned-row capacity exceeded: global max " +
                                             std::to_string(rows[1]) + " owned atoms, capacity " +
                                             std::to_string(c.max_owned));
+
+  // ev_setup: the per-atom arrays asked for start from zero over nlocal (+ nghost with newton).
+  double *eatom = (flags & LJX_EFLAG_ATOM) ? pair->eatom : nullptr;
+  double *vatom = (flags & LJX_VFLAG_ATOM) && !energy_only ? pair->vatom : nullptr;
+  const long long tally_rows =
+      static_cast<long long>(atoms->nlocal) + (newton_pair ? atoms->nghost : 0);
+  auto cs = static_cast<cudaStream_t>(stream);
+  if ((eatom && cudaMemsetAsync(eatom, 0, tally_rows * sizeof(double), cs) != cudaSuccess) ||
+      (vatom && cudaMemsetAsync(vatom, 0, 6 * tally_rows * sizeof(double), cs) != cudaSuccess))
+    return pair->fail(LJX_ERR_CUDA, "LAMMPS-JAX compute failed: per-atom arrays");
+  ljx_set_atom_tallies(e, eatom, vatom, pair->scale);
+  struct TalliesOff {
+    ljx_engine *e;
+    ~TalliesOff() { ljx_set_atom_tallies(e, nullptr, nullptr, 1.0); }
+  } tallies_off{e};
 
   if (ljx_pack_atoms(e, stream, atoms) != LJX_OK)
     return pair->fail(LJX_ERR_CAPACITY, ljx_engine_error(e));
@@ -319,6 +339,14 @@ ljx_status ljx_pair_tally(const ljx_pair *pair, double *eng_vdwl, double *virial
   if (eng_vdwl) *eng_vdwl = pair->eng_vdwl;
   if (virial)
     for (int k = 0; k < 6; ++k) virial[k] = pair->virial[k];
+  return LJX_OK;
+}
+
+ljx_status ljx_pair_set_atom_tallies(ljx_pair *pair, double *eatom, double *vatom)
+{
+  if (pair == nullptr) return LJX_ERR_INVALID;
+  pair->eatom = eatom;
+  pair->vatom = vatom;
   return LJX_OK;
 }
 

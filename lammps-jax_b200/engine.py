@@ -291,6 +291,12 @@ class PairJax:
     def init_one(self) -> float:
         return float(self.lib.ljx_pair_init_one(self._h))
 
+    def set_atom_tallies(self, eatom: torch.Tensor | None, vatom: torch.Tensor | None):
+        """Register LAMMPS's per-atom arrays (eatom [nmax] and vatom [nmax, 6] float64 device
+        tensors, or None) for computes with eflag_atom / vflag_atom."""
+        self._tallies = (eatom, vatom)  # kept alive while registered
+        self._check(self.lib.ljx_pair_set_atom_tallies(self._h, _ptr(eatom), _ptr(vatom)))
+
     def compute(self, system: System, eflag: bool = True, vflag: bool = True, stream=None, *,
                 eflag_atom: bool = False, vflag_atom: bool = False, eflag_only: bool = False):
         """One force evaluation; forces are added into system.f (ghost rows too, newton on).
