@@ -10,9 +10,11 @@ build recipe, ctypes binding, bundle writer/reader, a mirror of the reference pa
 from . import abi, build, md, synth  # noqa: F401
 from .abi import LjxError, load  # noqa: F401
 from .build import build_library  # noqa: F401
-from .bundle import Bundle, bundle_dict, eam_potential, lj_potential, write_bundle  # noqa: F401
+from .bundle import (Bundle, add_potential, bundle_dict, eam_potential,  # noqa: F401
+                     funcfl_potential, lj_potential, write_bundle)
 from .engine import Engine, LammpsError, NeighborList, PairJax, SelfComm, System  # noqa: F401
 
-__all__ = ["abi", "build", "md", "synth", "LjxError", "load", "build_library", "Bundle", "bundle_dict",
-           "eam_potential", "lj_potential", "write_bundle", "Engine", "LammpsError",
+__all__ = ["abi", "build", "md", "synth", "LjxError", "load", "build_library", "Bundle",
+           "add_potential", "bundle_dict", "eam_potential", "funcfl_potential", "lj_potential",
+           "write_bundle", "Engine", "LammpsError",
            "NeighborList", "PairJax", "SelfComm", "System"]

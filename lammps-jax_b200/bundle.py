@@ -96,6 +96,18 @@ def write_bundle(path, **kwargs) -> dict:
     return data
 
 
+def add_potential(path, potential: dict) -> dict:
+    """Insert the potential block into a bundle another exporter wrote (the reference's
+    export_model, python/lammps_jax/export.py:523-566, keeps its programs, contract and
+    export_info); the file is rewritten the way that exporter writes it (sorted keys, indent 2,
+    trailing newline). lammps-jax_b200/export_potential.patch makes the exporter itself take a
+    `potential=` argument instead."""
+    data = json.loads(Path(path).read_text(encoding="utf-8"))
+    data["potential"] = dict(potential)
+    Path(path).write_text(json.dumps(data, indent=2, sort_keys=True) + "\n", encoding="utf-8")
+    return data
+
+
 def _decode(value) -> str:
     return value.decode() if isinstance(value, bytes) else value
 

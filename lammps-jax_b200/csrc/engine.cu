@@ -58,6 +58,26 @@ int blocks_per_sm(Kernel kernel, int block = ljx::kBlock)
   return n;
 }
 
+// Shared-memory carveout preference (percent of the unified L1/shared array) of the force pass,
+// which uses almost no shared memory: 0 leaves the most L1 to its table and position gathers.
+// Negative: the driver's choice. Set once per kernel, before its occupancy is computed.
+#ifndef LJX_FORCE_CARVEOUT
+#define LJX_FORCE_CARVEOUT -1
+#endif
+template <typename Kernel>
+void prefer_carveout(Kernel kernel, int percent)
+{
+  if (percent < 0) return;
+  static std::mutex lock;
+  static std::unordered_map<const void *, bool> done;
+  const void *key = reinterpret_cast<const void *>(kernel);
+  std::lock_guard<std::mutex> guard(lock);
+  if (done.count(key)) return;
+  check(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, percent),
+        "cudaFuncSetAttribute(carveout)");
+  done.emplace(key, true);
+}
+
 }  // namespace
 
 struct ljx_bundle {
@@ -450,6 +470,9 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
 template <typename T, bool FORCES, bool TALLY>
 void launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
 {
+  prefer_carveout(ljx::k_force<T, ljx::kGhost, FORCES, TALLY>, LJX_FORCE_CARVEOUT);
+  prefer_carveout(ljx::k_force<T, ljx::kHalf, FORCES, TALLY>, LJX_FORCE_CARVEOUT);
+  prefer_carveout(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY>, LJX_FORCE_CARVEOUT);
   int grid = 0;
   switch (mode) {
     case ljx::kGhost:

@@ -227,7 +227,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
       xi = load4(p.xd4 + i);
       if (cached) {
         n = p.rcount[row];
-        slot0 = p.rslot[static_cast<long long>(row) * p.rcap + lane];
+        slot0 = load_once(p.rslot + static_cast<long long>(row) * p.rcap + lane);
       }
     }
     if (cached) {
@@ -263,7 +263,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
           if (base + lane < n) {
             // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
             // staged coordinates.
-            slot = base == 0 ? slot0 : slots[base + lane];
+            slot = base == 0 ? slot0 : load_once(slots + base + lane);
             xj = staged(s_xy, s_zw, slot);
             j = s_j[slot];
             r2d = pack_r2(xi, xj);

@@ -31,6 +31,10 @@ constexpr int kQueue = 64;
 #ifndef LJX_FORCE_MIN_BLOCKS
 #define LJX_FORCE_MIN_BLOCKS 4
 #endif
+// Pairs per lane and iteration of the double force pass (1 or 2).
+#ifndef LJX_FORCE_UNROLL
+#define LJX_FORCE_UNROLL 1
+#endif
 #if LJX_DENSITY_MIN_BLOCKS > 0
 #define LJX_DENSITY_BOUNDS __launch_bounds__(kBlock, LJX_DENSITY_MIN_BLOCKS)
 #else
@@ -66,6 +70,55 @@ __device__ __forceinline__ double4 load4(const double4 *p)
   return v;
 }
 __device__ __forceinline__ float4 load4(const float4 *p) { return __ldg(p); }
+
+// Spline-table rows: the tables (a few hundred KB in all) are re-read by every pair, while the
+// position and list data stream through L1; with LJX_L1_HINTS the table rows are kept in L1 in
+// preference (evict_last) and the once-read list words are dropped first (evict_first).
+#ifndef LJX_L1_HINTS
+#define LJX_L1_HINTS 0
+#endif
+__device__ __forceinline__ double4 load4_tab(const double4 *p)
+{
+#if LJX_L1_HINTS >= 1
+  double4 v;
+  asm("ld.global.nc.L1::evict_last.v4.f64 {%0, %1, %2, %3}, [%4];"
+      : "=d"(v.x), "=d"(v.y), "=d"(v.z), "=d"(v.w)
+      : "l"(p));
+  return v;
+#else
+  return load4(p);
+#endif
+}
+__device__ __forceinline__ float4 load4_tab(const float4 *p)
+{
+#if LJX_L1_HINTS >= 1
+  float4 v;
+  asm("ld.global.nc.L1::evict_last.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "l"(p));
+  return v;
+#else
+  return __ldg(p);
+#endif
+}
+template <typename W>
+__device__ __forceinline__ W load_once(const W *p)
+{
+#if LJX_L1_HINTS >= 2
+  static_assert(sizeof(W) == 4 || sizeof(W) == 2, "list words");
+  if constexpr (sizeof(W) == 4) {
+    unsigned v;
+    asm("ld.global.nc.L1::evict_first.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return *reinterpret_cast<W *>(&v);
+  } else {
+    unsigned short v;
+    asm("ld.global.nc.L1::evict_first.b16 %0, [%1];" : "=h"(v) : "l"(p));
+    return *reinterpret_cast<W *>(&v);
+  }
+#else
+  return __ldg(p);
+#endif
+}
 
 template <typename T>
 struct Step {
@@ -188,7 +241,7 @@ __device__ __forceinline__ void spline_vs(const typename Vec4<T>::type *tab, int
   T fl = floor(idx);
   fl = fmin(fmax(fl, T(0)), T(n - 2));
   const T t = fmin(idx - fl, T(1));
-  const auto c = load4(tab + static_cast<int>(fl));
+  const auto c = load4_tab(tab + static_cast<int>(fl));
   v = c.x + t * (c.y + t * (c.z + t * c.w));
   s = (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * inv_delta;
 }
@@ -200,7 +253,7 @@ __device__ __forceinline__ T spline_v(const typename Vec4<T>::type *tab, int n, 
   T fl = floor(idx);
   fl = fmin(fmax(fl, T(0)), T(n - 2));
   const T t = fmin(idx - fl, T(1));
-  const auto c = load4(tab + static_cast<int>(fl));
+  const auto c = load4_tab(tab + static_cast<int>(fl));
   return c.x + t * (c.y + t * (c.z + t * c.w));
 }
 
@@ -211,7 +264,7 @@ __device__ __forceinline__ T spline_s(const typename Vec4<T>::type *tab, int n, 
   T fl = floor(idx);
   fl = fmin(fmax(fl, T(0)), T(n - 2));
   const T t = fmin(idx - fl, T(1));
-  const auto c = load4(tab + static_cast<int>(fl));
+  const auto c = load4_tab(tab + static_cast<int>(fl));
   return (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * inv_delta;
 }
 
@@ -571,7 +624,7 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   const int node = static_cast<int>(fl);
   const T t = fmin(idx - fl, T(1));
   const int sj = static_cast<int>(pj.w);
-  const auto c = load4(p.pair + pair_row(si, sj) * p.nr + node);
+  const auto c = load4_tab(p.pair + pair_row(si, sj) * p.nr + node);
   const T z2 = c.x + t * (c.y + t * (c.z + t * c.w));
   const T phi = z2 * rinv;
   e += static_cast<double>(phi);
@@ -581,7 +634,7 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
       atomicAdd(p.eatom + j, p.tally_scale * 0.5 * static_cast<double>(phi));
   }
   if constexpr (FORCES) {
-    const auto dj = load4(p.density_slope + sj * p.nr + node);
+    const auto dj = load4_tab(p.density_slope + sj * p.nr + node);
     const T rhojp = dj.x + t * (dj.y + t * dj.z);
     const T z2p = (c.y + t * (T(2) * c.z + t * (T(3) * c.w))) * p.inv_dr;
     const T phip = (z2p - phi) * rinv;
@@ -591,7 +644,7 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
     } else if (si == sj) {
       psip = (fpi + fpj) * rhojp + phip;
     } else {
-      const auto di = load4(p.density_slope + si * p.nr + node);
+      const auto di = load4_tab(p.density_slope + si * p.nr + node);
       psip = fpi * rhojp + fpj * (di.x + t * (di.y + t * di.z)) + phip;
     }
     const T sc = psip * rinv;
@@ -705,10 +758,26 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
     }
     if (n <= p.row_cap) {
       const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
-      if constexpr (sizeof(T) == 8) {
+      if constexpr (sizeof(T) == 8 && LJX_FORCE_UNROLL == 2) {
+        // Two independent pairs per lane and iteration: both pairs' position and F' gathers,
+        // then both table lookups, are in flight together.
+        for (int k = lane; k < n; k += 2 * kWarp) {
+          const int k2 = k + kWarp;
+          const bool two = k2 < n;
+          const int j = load_once(crow + k);
+          const int j2 = two ? load_once(crow + k2) : j;
+          const V pj = load_pos(p, j), pj2 = load_pos(p, j2);
+          const T fpj = kNeedFpj ? __ldg(p.fp + j) : T(0);
+          const T fpj2 = kNeedFpj ? __ldg(p.fp + j2) : T(0);
+          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v, er, vr);
+          if (two)
+            eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j2, pj2, fpj2, fx, fy, fz, e, v, er,
+                                             vr);
+        }
+      } else if constexpr (sizeof(T) == 8) {
         // (Pipelining as below spills at 64 registers in double runs and loses.)
         for (int k = lane; k < n; k += kWarp) {
-          const int j = crow[k];
+          const int j = load_once(crow + k);
           eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, load_pos(p, j),
                                            kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
                                            er, vr);
@@ -722,7 +791,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
         V pj = V{};
         T fpj = T(0);
         if (k < n) {
-          j = crow[k];
+          j = load_once(crow + k);
           pj = load_pos(p, j);
           if (kNeedFpj) fpj = __ldg(p.fp + j);
         }
@@ -732,7 +801,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
           V pj2 = V{};
           T fpj2 = T(0);
           if (k2 < n) {
-            j2 = crow[k2];
+            j2 = load_once(crow + k2);
             pj2 = load_pos(p, j2);
             if (kNeedFpj) fpj2 = __ldg(p.fp + j2);
           }
