@@ -62,7 +62,7 @@ int blocks_per_sm(Kernel kernel, int block = ljx::kBlock)
 // which uses almost no shared memory: 0 leaves the most L1 to its table and position gathers.
 // Negative: the driver's choice. Set once per kernel, before its occupancy is computed.
 #ifndef LJX_FORCE_CARVEOUT
-#define LJX_FORCE_CARVEOUT -1
+#define LJX_FORCE_CARVEOUT 0
 #endif
 template <typename Kernel>
 void prefer_carveout(Kernel kernel, int percent)
@@ -451,17 +451,21 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   if (rebuild) e->group_builds++;
   e->groups_valid = true;
   e->groups_key = key;
-  int grid = 0;
   const int need = groups;  // one block per group
-  if (mode == ljx::kDensityHalf) {
-    grid = std::max(1, std::min(need, std::min(e->max_grid, e->sm_count * blocks_per_sm(
-                                                            ljx::k_density_groups<T, ljx::kDensityHalf>))));
-    ljx::k_density_groups<T, ljx::kDensityHalf><<<grid, ljx::kBlock, 0, s>>>(p);
-  } else {
-    grid = std::max(1, std::min(need, std::min(e->max_grid, e->sm_count * blocks_per_sm(
-                                                            ljx::k_density_groups<T, ljx::kDensityFull>))));
-    ljx::k_density_groups<T, ljx::kDensityFull><<<grid, ljx::kBlock, 0, s>>>(p);
-  }
+  const bool rules = p.half_rule || p.unique_rule;
+  auto run = [&](auto kernel) {
+    const int grid = std::max(1, std::min(need, std::min(e->max_grid,
+                                                         e->sm_count * blocks_per_sm(kernel))));
+    kernel<<<grid, ljx::kBlock, 0, s>>>(p);
+    return grid;
+  };
+  int grid = 0;
+  if (mode == ljx::kDensityHalf)
+    grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityHalf, true>)
+                 : run(ljx::k_density_groups<T, ljx::kDensityHalf, false>);
+  else
+    grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityFull, true>)
+                 : run(ljx::k_density_groups<T, ljx::kDensityFull, false>);
   check_launch("k_density_groups");
   e->launches++;
   e->step_blocks[kDensityPart] = grid;
@@ -470,22 +474,17 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
 template <typename T, bool FORCES, bool TALLY>
 void launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
 {
-  prefer_carveout(ljx::k_force<T, ljx::kGhost, FORCES, TALLY>, LJX_FORCE_CARVEOUT);
-  prefer_carveout(ljx::k_force<T, ljx::kHalf, FORCES, TALLY>, LJX_FORCE_CARVEOUT);
-  prefer_carveout(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY>, LJX_FORCE_CARVEOUT);
+  auto run = [&](auto kernel) {
+    prefer_carveout(kernel, LJX_FORCE_CARVEOUT);
+    const int grid = row_grid(e, p.inum, blocks_per_sm(kernel));
+    kernel<<<grid, ljx::kBlock, 0, s>>>(p);
+    return grid;
+  };
   int grid = 0;
   switch (mode) {
-    case ljx::kGhost:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kGhost, FORCES, TALLY>));
-      ljx::k_force<T, ljx::kGhost, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
-      break;
-    case ljx::kHalf:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kHalf, FORCES, TALLY>));
-      ljx::k_force<T, ljx::kHalf, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
-      break;
-    default:
-      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY>));
-      ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY><<<grid, ljx::kBlock, 0, s>>>(p);
+    case ljx::kGhost: grid = run(ljx::k_force<T, ljx::kGhost, FORCES, TALLY>); break;
+    case ljx::kHalf: grid = run(ljx::k_force<T, ljx::kHalf, FORCES, TALLY>); break;
+    default: grid = run(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY>);
   }
   check_launch("k_force");
   e->launches++;
@@ -497,10 +496,11 @@ void launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode
 {
   if (p.inum <= 0) return;
   // The per-atom tally variants run only when a caller asked for per-atom output.
-  if (p.eatom != nullptr || p.vatom != nullptr)
+  if (p.eatom != nullptr || p.vatom != nullptr) {
     launch_force_as<T, FORCES, true>(e, s, p, mode);
-  else
-    launch_force_as<T, FORCES, false>(e, s, p, mode);
+    return;
+  }
+  launch_force_as<T, FORCES, false>(e, s, p, mode);
 }
 
 template <typename T, bool FORCES, bool TALLY>

@@ -195,7 +195,9 @@ __device__ __forceinline__ double4 staged(const double2 *xy, const double2 *zw, 
 // keep test, compacts the kept pairs into the row's segment of the compacted buffer (the force
 // pass reads it as from k_density) and accumulates the EAM density, scattered to the neighbor as
 // well for half lists. Groups past capacity walk their rows' lists.
-template <typename T, int MODE>
+// RULES: the bundle's packing has a half or unique-boundary rule to apply (half-edge bundles on
+// a full list); without one the keep test is the distance alone.
+template <typename T, int MODE, bool RULES = true>
 __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
 {
   // Staged positions as two 16-byte halves: consecutive slots then fall on different bank
@@ -265,12 +267,17 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
             // staged coordinates.
             slot = base == 0 ? slot0 : load_once(slots + base + lane);
             xj = staged(s_xy, s_zw, slot);
-            j = s_j[slot];
             r2d = pack_r2(xi, xj);
-            keep = r2d <= p.pack_cutsq && pair_rules(p, i, xi, j, xj);
+            if constexpr (RULES) {
+              j = s_j[slot];
+              keep = r2d <= p.pack_cutsq && pair_rules(p, i, xi, j, xj);
+            } else {
+              keep = r2d <= p.pack_cutsq;
+            }
           }
           const unsigned m = __ballot_sync(kFull, keep);
           if (keep) {
+            if constexpr (!RULES) j = s_j[slot];
             const int at = kept + __popc(m & below);
             if (at < p.row_cap) crow[at] = j;
             T r2;

@@ -31,10 +31,6 @@ constexpr int kQueue = 64;
 #ifndef LJX_FORCE_MIN_BLOCKS
 #define LJX_FORCE_MIN_BLOCKS 4
 #endif
-// Pairs per lane and iteration of the double force pass (1 or 2).
-#ifndef LJX_FORCE_UNROLL
-#define LJX_FORCE_UNROLL 1
-#endif
 #if LJX_DENSITY_MIN_BLOCKS > 0
 #define LJX_DENSITY_BOUNDS __launch_bounds__(kBlock, LJX_DENSITY_MIN_BLOCKS)
 #else
@@ -75,7 +71,7 @@ __device__ __forceinline__ float4 load4(const float4 *p) { return __ldg(p); }
 // position and list data stream through L1; with LJX_L1_HINTS the table rows are kept in L1 in
 // preference (evict_last) and the once-read list words are dropped first (evict_first).
 #ifndef LJX_L1_HINTS
-#define LJX_L1_HINTS 0
+#define LJX_L1_HINTS 2
 #endif
 __device__ __forceinline__ double4 load4_tab(const double4 *p)
 {
@@ -458,8 +454,9 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
       int q = 0;     // pairs waiting in the queue
       // Write out kept pair (i -> j) at `slot` of the compacted row and add its density.
       auto evaluate = [&](int slot, int j, float r2f) {
-        if (slot < p.row_cap) crow[slot] = j;
-        if (MODE != kCompactOnly) {
+        if (MODE == kCompactOnly) {
+          if (slot < p.row_cap) crow[slot] = j;
+        } else {
           T r2;
           int sj;
           if constexpr (sizeof(T) == 8) {
@@ -471,6 +468,7 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
             r2 = r2f;
             sj = static_cast<int>(__ldg(&pos4f[j].w));
           }
+          if (slot < p.row_cap) crow[slot] = j;
           if (r2 < p.model_cutsq) {
             const T r = sqrt(r2);
             rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
@@ -597,8 +595,8 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
   store_partials(acc, 0, p.partials);
 }
 
-// One EAM edge (i -> j) of the force pass; python/lammps_jax/eam.py:383-398 for the pair force
-// and :300-309 for the pair energy. r and 1/r come from one reciprocal square root; the density
+// One EAM edge (i -> j, neighbor species sj) of the force pass; python/lammps_jax/eam.py:383-398
+// for the pair force and :300-309 for the pair energy. r and 1/r come from one reciprocal square root; the density
 // and pair tables share the r grid, so one (node, t) serves both lookups; F' of the density
 // comes from the pre-scaled slope table. Accumulates the row force and the thread's pair energy
 // and virial (both without their constant weights, applied once per block). Without FORCES only
@@ -611,8 +609,8 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
 template <typename T, int MODE, bool FORCES = true, bool TALLY = false>
 __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T>::type &pi,
                                          int si, T fpi, int j, const typename Vec4<T>::type &pj,
-                                         T fpj, T &fx, T &fy, T &fz, double &e, double (&v)[6],
-                                         double &er, double (&vr)[6])
+                                         int sj, T fpj, T &fx, T &fy, T &fz, double &e,
+                                         double (&v)[6], double &er, double (&vr)[6])
 {
   const T dx = pj.x - pi.x, dy = pj.y - pi.y, dz = pj.z - pi.z;
   const T r2 = dx * dx + dy * dy + dz * dz;
@@ -623,7 +621,6 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   const T fl = fmin(floor(idx), T(p.nr - 2));
   const int node = static_cast<int>(fl);
   const T t = fmin(idx - fl, T(1));
-  const int sj = static_cast<int>(pj.w);
   const auto c = load4_tab(p.pair + pair_row(si, sj) * p.nr + node);
   const T z2 = c.x + t * (c.y + t * (c.z + t * c.w));
   const T phi = z2 * rinv;
@@ -758,27 +755,12 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
     }
     if (n <= p.row_cap) {
       const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
-      if constexpr (sizeof(T) == 8 && LJX_FORCE_UNROLL == 2) {
-        // Two independent pairs per lane and iteration: both pairs' position and F' gathers,
-        // then both table lookups, are in flight together.
-        for (int k = lane; k < n; k += 2 * kWarp) {
-          const int k2 = k + kWarp;
-          const bool two = k2 < n;
-          const int j = load_once(crow + k);
-          const int j2 = two ? load_once(crow + k2) : j;
-          const V pj = load_pos(p, j), pj2 = load_pos(p, j2);
-          const T fpj = kNeedFpj ? __ldg(p.fp + j) : T(0);
-          const T fpj2 = kNeedFpj ? __ldg(p.fp + j2) : T(0);
-          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v, er, vr);
-          if (two)
-            eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j2, pj2, fpj2, fx, fy, fz, e, v, er,
-                                             vr);
-        }
-      } else if constexpr (sizeof(T) == 8) {
+      if constexpr (sizeof(T) == 8) {
         // (Pipelining as below spills at 64 registers in double runs and loses.)
         for (int k = lane; k < n; k += kWarp) {
           const int j = load_once(crow + k);
-          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, load_pos(p, j),
+          const V pj = load_pos(p, j);
+          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
                                            kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
                                            er, vr);
         }
@@ -805,8 +787,8 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
             pj2 = load_pos(p, j2);
             if (kNeedFpj) fpj2 = __ldg(p.fp + j2);
           }
-          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, fpj, fx, fy, fz, e, v, er,
-                                           vr);
+          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w), fpj,
+                                           fx, fy, fz, e, v, er, vr);
           k = k2;
           j = j2;
           pj = pj2;
@@ -820,10 +802,12 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
       for (int jj = lane; jj < listed; jj += kWarp) {
         const int j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
         if (j >= p.max_atoms) continue;
-        if (pack_keep(p, i, xi, j, load4(p.xd4 + j)))
-          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, load_pos(p, j),
+        if (pack_keep(p, i, xi, j, load4(p.xd4 + j))) {
+          const V pj = load_pos(p, j);
+          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
                                            kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
                                            er, vr);
+        }
       }
     }
     if constexpr (FORCES) {
