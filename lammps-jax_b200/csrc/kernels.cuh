@@ -199,6 +199,24 @@ __device__ __forceinline__ float warp_sum(float v)
   return v;
 }
 
+// Warp sums of three per-lane values in 6 exchange steps instead of 15. The first step swaps
+// half of (a, b) / (c, 0) between the two half-warps, the second keeps one of the two remaining
+// partials per quarter; afterwards each group of 8 lanes sums one of a, b, c, 0. The total of a
+// is in lane 0, of b in lane 8 and of c in lane 16.
+template <typename T>
+__device__ __forceinline__ T warp_sum3(T a, T b, T c, int lane)
+{
+  const bool hi16 = (lane & 16) != 0;
+  const T k0 = (hi16 ? c : a) + __shfl_xor_sync(kFull, hi16 ? a : c, 16);
+  const T k1 = (hi16 ? T(0) : b) + __shfl_xor_sync(kFull, hi16 ? b : T(0), 16);
+  const bool hi8 = (lane & 8) != 0;
+  T m = (hi8 ? k1 : k0) + __shfl_xor_sync(kFull, hi8 ? k0 : k1, 8);
+  m += __shfl_xor_sync(kFull, m, 4);
+  m += __shfl_xor_sync(kFull, m, 2);
+  m += __shfl_xor_sync(kFull, m, 1);
+  return m;
+}
+
 // Reduce the thread's {energy, virial[6], kept} sums and widest row over the block and store
 // one partial row (every slot written, so the finalize step can sum all kernels uniformly).
 __device__ __forceinline__ void store_partials(double (&v)[8], int widest, double *partials)
@@ -811,20 +829,14 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
       }
     }
     if constexpr (FORCES) {
-      fx = warp_sum(fx);
-      fy = warp_sum(fy);
-      fz = warp_sum(fz);
-      if (lane == 0 && i < p.nall) {
-        double *fi = p.f + 3 * i;
-        if (MODE == kRowsFull) {
-          fi[0] += p.scale * static_cast<double>(fx);
-          fi[1] += p.scale * static_cast<double>(fy);
-          fi[2] += p.scale * static_cast<double>(fz);
-        } else {
-          atomicAdd(fi + 0, p.scale * static_cast<double>(fx));
-          atomicAdd(fi + 1, p.scale * static_cast<double>(fy));
-          atomicAdd(fi + 2, p.scale * static_cast<double>(fz));
-        }
+      // The row force: x in lane 0, y in lane 8, z in lane 16, each stored by its lane.
+      const T fc = warp_sum3(fx, fy, fz, lane);
+      if ((lane & 7) == 0 && lane < 24 && i < p.nall) {
+        double *fi = p.f + 3 * i + (lane >> 3);
+        if (MODE == kRowsFull)
+          *fi += p.scale * static_cast<double>(fc);
+        else
+          atomicAdd(fi, p.scale * static_cast<double>(fc));
       }
     }
     if constexpr (TALLY) tally_row<T, MODE == kRowsFull>(p, lane, i, er, vr);
