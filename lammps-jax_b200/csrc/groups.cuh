@@ -289,7 +289,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
               r2 = dx * dx + dy * dy + dz * dz;
             }
             if (r2 < p.model_cutsq) {
-              const T r = sqrt(r2);
+              const T r = pair_distance(r2);
               const int sj = static_cast<int>(xj.w);
               rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
               if (MODE == kDensityHalf)
@@ -327,7 +327,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
               r2 = dx * dx + dy * dy + dz * dz;
             }
             if (r2 < p.model_cutsq) {
-              const T r = sqrt(r2);
+              const T r = pair_distance(r2);
               rho += spline_v<T>(p.density + static_cast<int>(xj.w) * p.nr, p.nr, r, p.inv_dr);
               if (MODE == kDensityHalf)
                 atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
