@@ -463,6 +463,8 @@ def run_ljx(args):
     case.close()
     del case, system, decomp
     torch.cuda.empty_cache()
+    if world == 1 and not args.skip_extras and args.config == "c3" and precision == "float64":
+        line["c3_f32"] = run_c3_f32(ljx, args, local)
     if not args.skip_extras and not args.no_c4 and args.config == "c3":
         line["c4"] = run_c4(ljx, args, world, rank, local)
     if world == 1 and not args.skip_extras and args.config == "c3":
@@ -473,6 +475,25 @@ def run_ljx(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_c3_f32(ljx, args, local):
+    """C3 in float32, the other precision the configuration names: the same crystal, list and
+    step, timed the same way on the device."""
+    import torch
+    case = Case(ljx, "c3", "float32", 1, 0, local, args.cells)
+    timing = case.time(args.steps, args.warmup, args.rebuild_every)
+    energy = timing["result"][0]
+    out = {"precision": "float32", "total_atoms": case.nlocal, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": timing["elapsed"] / args.steps * 1e3,
+           "value": case.nlocal * args.steps / timing["elapsed"], "unit": UNIT,
+           "gpu_launches": timing["launches"],
+           "phase_ms": {n: v * 1e3 for n, v in timing["phase"].items()},
+           "energy_per_atom": energy / case.nlocal}
+    case.close()
+    del case
+    torch.cuda.empty_cache()
+    return out
 
 
 C4_SAMPLES = 16
