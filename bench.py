@@ -220,9 +220,17 @@ class Case:
         self.stream = torch.cuda.current_stream()
         self.tick = 0
 
-    def core(self, ago, mark=lambda k: None):
+    def streams_rows(self):
+        """Whether the force pass can stream its rows to the host (each list row holds its
+        atom's whole force: full list, newton off)."""
+        return not self.system.newton_pair and not self.system.list.half
+
+    def core(self, ago, mark=lambda k: None, f_host=None, pieces=8, ev=True):
         """One pair-style step on device data, with the exchanges the engine's plan asks for.
-        Returns (energy, virial, kept edges, overflow) over all ranks."""
+        With f_host (pinned, nlocal x 3) the force pass streams the owned force rows to it
+        piece by piece (ljx_force_to_host). Without ev the step computes forces alone
+        (ljx_force_only: LAMMPS's steps between thermo output). Returns (energy, virial, kept
+        edges, overflow) over all ranks."""
         s, eng, atoms, nl = self.system, self.eng, self.atoms, self.nl
         newton = s.newton_pair
         nl.ago = ago
@@ -238,7 +246,12 @@ class Case:
         if self.plan.forward_fp:
             s.comm.forward(self.fp_rows, self.width, self.elem)
         mark(4)
-        eng.force(atoms, nl, newton, 1.0)
+        if f_host is not None:
+            eng.force_to_host(atoms, nl, newton, f_host, 1.0, pieces)
+        elif not ev:
+            eng.force_only(atoms, nl, newton, 1.0)
+        else:
+            eng.force(atoms, nl, newton, 1.0)
         if self.plan.reverse_force:
             s.comm.reverse_forces(s.f)  # LAMMPS's own reverse comm of ghost forces
         mark(5)
@@ -254,7 +267,7 @@ class Case:
         mark(6)
         return out
 
-    def step(self, rebuild_every, events=None):
+    def step(self, rebuild_every, events=None, ev=True):
         def mark(k):
             if events is not None:
                 events[k].record(self.stream)
@@ -262,14 +275,15 @@ class Case:
         # engine rebuilds its candidate cache on ago == 0 (-1: cache off).
         ago = self.tick % rebuild_every if rebuild_every > 0 else -1
         self.tick += 1
-        return self.core(ago, mark)
+        return self.core(ago, mark, ev=ev)
 
     def launches(self):
         return self.eng.launches + (self.halo.launches if self.halo is not None else 0)
 
-    def time(self, steps, warmup, rebuild_every):
+    def time(self, steps, warmup, rebuild_every, ev=True):
         """Warm up, then time `steps` steps with CUDA events on the launching stream, bracketed
-        by a barrier and a device synchronize; the max over ranks."""
+        by a barrier and a device synchronize; the max over ranks. Without ev: force-only
+        steps."""
         import torch
         import torch.distributed as dist
         names = ["pack_atoms", "density", "embed", "halo_fp", "force", "result"]
@@ -278,14 +292,14 @@ class Case:
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         out = None
         for _ in range(warmup):
-            out = self.step(rebuild_every)
+            out = self.step(rebuild_every, ev=ev)
         torch.cuda.synchronize()
         if self.world > 1:
             dist.barrier()
         launches0 = self.launches()
         start.record(self.stream)
         for k in range(steps):
-            out = self.step(rebuild_every, kevents[k])
+            out = self.step(rebuild_every, kevents[k], ev=ev)
         stop.record(self.stream)
         torch.cuda.synchronize()
         elapsed = start.elapsed_time(stop) / 1e3
@@ -406,6 +420,16 @@ def run_ljx(args):
     total_atoms = case.total_atoms()
     neigh_ms = time_list_build(torch, decomp["lists"], system.x, case.stream)
     e2e = None if args.skip_extras else run_e2e(torch, case, args, world, total_atoms)
+    force_only = None
+    if not args.skip_extras:
+        # LAMMPS asks for energy and virial on thermo steps only; the steps between run the
+        # forces alone (ljx_force_only, the reference's force program).
+        fo = case.time(args.steps, args.warmup, args.rebuild_every, ev=False)
+        force_only = {"what": "steps without energy or virial (LAMMPS steps between thermo "
+                              "output; ljx_force_only)",
+                      "value": total_atoms * args.steps / fo["elapsed"], "unit": UNIT,
+                      "ms_per_step": fo["elapsed"] / args.steps * 1e3,
+                      "phase_ms": {n: v * 1e3 for n, v in fo["phase"].items()}}
     value = total_atoms * args.steps / elapsed
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -457,17 +481,20 @@ def run_ljx(args):
         "e2e": e2e,
         "energy_per_atom": energy_total / total_atoms,
     }
-    if world == 1 and not args.skip_extras and args.config == "c3":
+    if force_only is not None:
+        line["force_only"] = force_only
+    extras = not args.skip_extras and not args.quick
+    if world == 1 and extras and args.config == "c3":
         line["md"] = run_md(torch, ljx, cfg, case.cells, precision, args.steps, args.warmup)
     line["clocks"] = clocks.summary()
     case.close()
     del case, system, decomp
     torch.cuda.empty_cache()
-    if world == 1 and not args.skip_extras and args.config == "c3" and precision == "float64":
+    if world == 1 and extras and args.config == "c3" and precision == "float64":
         line["c3_f32"] = run_c3_f32(ljx, args, local)
-    if not args.skip_extras and not args.no_c4 and args.config == "c3":
+    if extras and not args.no_c4 and args.config == "c3":
         line["c4"] = run_c4(ljx, args, world, rank, local)
-    if world == 1 and not args.skip_extras and args.config == "c3":
+    if world == 1 and extras and args.config == "c3":
         line["cpu_baseline"] = cpu_baseline(args)
     if world > 1:
         dist.barrier()
@@ -704,6 +731,7 @@ def run_e2e(torch, case, args, world, total_atoms):
     stream = case.stream
     steps = max(3, min(args.steps, 10))
     lib = package().abi.load()
+    streamed = args.e2e_pieces > 0 and case.streams_rows()
 
     def one(k):
         if owned_only:
@@ -719,9 +747,15 @@ def run_e2e(torch, case, args, world, total_atoms):
             system.x.copy_(x_host, non_blocking=True)
         if k % period == 0:
             lists.launch(system.x, stream)
-        case.core(k % period if args.rebuild_every > 0 else -1)  # ends with the result read
-        f_host.copy_(system.f[:nlocal], non_blocking=True)
-        stream.synchronize()                                    # forces on the host
+        ago = k % period if args.rebuild_every > 0 else -1
+        if streamed:
+            # The force rows go to the host piece by piece under the force pass; the result
+            # read that ends the step waits for the last piece.
+            case.core(ago, f_host=f_host, pieces=args.e2e_pieces)
+        else:
+            case.core(ago)  # ends with the result read
+            f_host.copy_(system.f[:nlocal], non_blocking=True)
+            stream.synchronize()                                # forces on the host
         return x_host.numel() * 8
 
     one(1)
@@ -747,7 +781,10 @@ def run_e2e(torch, case, args, world, total_atoms):
                          if owned_only else "owned and ghost rows"),
             "list": ("rebuilt on the device every step from the uploaded positions" if period == 1
                      else f"rebuilt on the device every {period}th step from the uploaded "
-                          "positions")}
+                          "positions"),
+            "f_download": (f"streamed under the force pass in {args.e2e_pieces} row pieces "
+                           "(ljx_force_to_host)" if streamed
+                           else "one copy after the step")}
 
 
 def reference_sample(ljx, oracle, args):
@@ -876,6 +913,12 @@ def main():
                          "profiling")
     ap.add_argument("--no-c4", action="store_true",
                     help="leave out the C4 strong-scaling object of the c3 line")
+    ap.add_argument("--e2e-pieces", type=int, default=8,
+                    help="row pieces of the e2e force pass whose force rows are copied to the "
+                         "host as each finishes (ljx_force_to_host); 0: one copy after the step")
+    ap.add_argument("--quick", action="store_true",
+                    help="time the device path, the e2e and the force-only legs only (no MD, "
+                         "C4, float32 or CPU-baseline legs)")
     args = ap.parse_args()
     if args.precision is None:
         args.precision = CONFIGS[args.config].get("precision", "float64")

@@ -196,6 +196,31 @@ ljx_status ljx_embed(ljx_engine *engine, void *stream, const ljx_atoms *atoms);
 ljx_status ljx_force(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
                      const ljx_list *list, int newton_pair, double scale);
 
+/* Forces alone: the reference's execute_force path, which LAMMPS takes on every step that asks
+ * for neither energy nor virial (cpp/pair_jax_kokkos.cpp:1002-1003, 1055-1057, 1092; eflag and vflag
+ * are set only on thermo steps). The forces of ljx_force (to the last bit: without the sums the
+ * compiler may fuse a multiply-add the full pass keeps apart) from an EAM force pass that sums no
+ * pair energy and no virial (fewer registers per thread); LJ runs its one pass as in ljx_force. The next ljx_read_result / ljx_read_result_all reports energy and virial as zero and
+ * the edge count and overflow as usual. Per-atom tallies, when registered, run the full pass. */
+ljx_status ljx_force_only(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
+                          const ljx_list *list, int newton_pair, double scale);
+
+/* ljx_force with the owned force rows streamed to host memory while the pass runs: the pass is
+ * launched as `pieces` (1..16) consecutive ranges of list rows, and each range's rows of
+ * atoms->f are copied to f_host (double[nlocal][3], pinned host memory for the copies to overlap)
+ * on an engine-owned copy stream as soon as that range has finished, so the device-to-host copy
+ * of a LAMMPS step's forces (atomKK->sync of f to the host) runs under the rest of the pass.
+ * `stream` is ordered after the last copy when this returns, so a synchronize of it (ljx_read_result
+ * does one) leaves f_host complete: atoms->f as ljx_force leaves it, rows 0..nlocal-1.
+ * Only where a list row holds its atom's whole force: EAM full list with newton off, LJ
+ * edge-force bundles on a full list (otherwise LJX_ERR_UNSUPPORTED, nothing launched). Row r of
+ * the list must be atom r (ilist[r] == r, as LAMMPS's Kokkos lists are built); a device check
+ * runs with the pass and the next ljx_read_result / ljx_read_result_all fails with
+ * LJX_ERR_INVALID if a row was out of order (f_host is then not usable; atoms->f is). */
+ljx_status ljx_force_to_host(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
+                             const ljx_list *list, int newton_pair, double scale, double *f_host,
+                             int pieces);
+
 /* Energy-only evaluation: the reference's execute_energy path for LAMMPS eflag_only steps (MC
  * moves; cpp/pair_jax_kokkos.cpp:997-1001, 1051-1053, runtime execute_energy). After ljx_density
  * and ljx_embed (and the reverse rho exchange of half-list plans) it sums the pair energy (EAM)

@@ -110,6 +110,10 @@ SIGNATURES = [
     ("ljx_embed", c_int, [c_void_p, c_void_p, POINTER(Atoms)]),
     ("ljx_force", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
                           c_double]),
+    ("ljx_force_only", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
+                               c_double]),
+    ("ljx_force_to_host", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
+                                  c_double, c_void_p, c_int]),
     ("ljx_energy", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
                            c_double]),
     ("ljx_read_result", c_int, [c_void_p, c_void_p, POINTER(Result)]),

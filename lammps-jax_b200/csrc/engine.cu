@@ -151,11 +151,23 @@ struct ljx_engine {
   double *vatom = nullptr;
   double tally_scale = 1.0;
   long long launches = 0;
+  // ljx_force_to_host: the copy stream and the events that order it after each piece of the
+  // force pass; the row-order check word (device, and its pinned landing slot) and whether this
+  // step's result read must look at it.
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t piece_done[17] = {};
+  int *order_bad = nullptr;       // device: rows r with ilist[r] != r (result slot 12)
+  int *host_order_bad = nullptr;  // pinned: its copy (host_result slot 12)
+  bool rows_streamed = false;
+  bool step_ev = true;            // false after ljx_force_only: the result has no energy/virial
   std::string error;
 
   ~ljx_engine()
   {
     cudaSetDevice(device);
+    for (cudaEvent_t ev : piece_done)
+      if (ev) cudaEventDestroy(ev);
+    if (copy_stream) cudaStreamDestroy(copy_stream);
     void *ptrs[] = {xd4,       pos4,      rho,        fp,          cedges,  ccount,
                     embedding, density,   density_slope, pair,     coord_bound, xref,
                     gatom,     gcount,    rslot,      rcount,      senders,
@@ -471,36 +483,41 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   e->step_blocks[kDensityPart] = grid;
 }
 
-template <typename T, bool FORCES, bool TALLY>
-void launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+// block0 / cap: a pass launched in pieces (ljx_force_to_host) writes its partial rows after
+// those of the earlier pieces, at most `cap` blocks (0: no cap).
+template <typename T, bool FORCES, bool TALLY, bool EV = true>
+int launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode,
+                    int block0 = 0, int cap = 0)
 {
   auto run = [&](auto kernel) {
     prefer_carveout(kernel, LJX_FORCE_CARVEOUT);
-    const int grid = row_grid(e, p.inum, blocks_per_sm(kernel));
+    int grid = row_grid(e, p.inum, blocks_per_sm(kernel));
+    if (cap > 0) grid = std::min(grid, cap);
     kernel<<<grid, ljx::kBlock, 0, s>>>(p);
     return grid;
   };
   int grid = 0;
   switch (mode) {
-    case ljx::kGhost: grid = run(ljx::k_force<T, ljx::kGhost, FORCES, TALLY>); break;
-    case ljx::kHalf: grid = run(ljx::k_force<T, ljx::kHalf, FORCES, TALLY>); break;
-    default: grid = run(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY>);
+    case ljx::kGhost: grid = run(ljx::k_force<T, ljx::kGhost, FORCES, TALLY, EV>); break;
+    case ljx::kHalf: grid = run(ljx::k_force<T, ljx::kHalf, FORCES, TALLY, EV>); break;
+    default: grid = run(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY, EV>);
   }
   check_launch("k_force");
   e->launches++;
-  e->step_blocks[kForcePart] = grid;
+  // A force-only pass writes no partial sums.
+  e->step_blocks[kForcePart] = EV ? block0 + grid : 0;
+  return grid;
 }
 
 template <typename T, bool FORCES = true>
-void launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode)
+int launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode, int block0 = 0,
+                 int cap = 0)
 {
-  if (p.inum <= 0) return;
+  if (p.inum <= 0) return 0;
   // The per-atom tally variants run only when a caller asked for per-atom output.
-  if (p.eatom != nullptr || p.vatom != nullptr) {
-    launch_force_as<T, FORCES, true>(e, s, p, mode);
-    return;
-  }
-  launch_force_as<T, FORCES, false>(e, s, p, mode);
+  if (p.eatom != nullptr || p.vatom != nullptr)
+    return launch_force_as<T, FORCES, true>(e, s, p, mode, block0, cap);
+  return launch_force_as<T, FORCES, false>(e, s, p, mode, block0, cap);
 }
 
 template <typename T, bool FORCES, bool TALLY>
@@ -633,6 +650,7 @@ ljx_status force_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const l
   ljx::Step<T> p = make_step<T>(e, a, l, scale);
   set_pack_rules(p, e->c, m);
   e->last_scale = scale;
+  e->step_ev = true;
   if (e->c.potential == LJX_POTENTIAL_LJ) {
     p.partials = e->partial(kLjPart);
     launch_lj<T>(e, s, p, m.lj);
@@ -641,6 +659,116 @@ ljx_status force_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const l
   }
   p.partials = e->partial(kForcePart);
   launch_force<T>(e, s, p, m.force);
+  return LJX_OK;
+}
+
+// Forces alone (ljx_force_only): the EAM force pass without its energy and virial sums; LJ runs
+// its one pass as ljx_force does. The step's result then reports no energy or virial.
+template <typename T>
+ljx_status force_only_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
+                           int newton_pair, double scale)
+{
+  if (e->c.potential == LJX_POTENTIAL_LJ || e->eatom != nullptr || e->vatom != nullptr) {
+    const ljx_status st = force_impl<T>(e, s, a, l, newton_pair, scale);
+    e->step_ev = false;
+    return st;
+  }
+  const Modes m = decide_modes(e->c, newton_pair);
+  ljx::Step<T> p = make_step<T>(e, a, l, scale);
+  set_pack_rules(p, e->c, m);
+  e->last_scale = scale;
+  p.partials = e->partial(kForcePart);
+  if (p.inum > 0) launch_force_as<T, true, false, false>(e, s, p, m.force);
+  e->step_ev = false;
+  return LJX_OK;
+}
+
+// Rows r of the list whose atom is not r (ljx_force_to_host copies atom ranges by row ranges).
+__global__ void k_rows_in_order(const int *ilist, int inum, int *bad)
+{
+  int count = 0;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < inum; r += gridDim.x * blockDim.x)
+    count += ilist[r] != r;
+  count = __reduce_add_sync(0xffffffffu, static_cast<unsigned>(count));
+  if ((threadIdx.x & 31) == 0 && count) atomicAdd(bad, count);
+}
+
+// The force pass in `pieces` consecutive row ranges; after each, its owned rows of f go to the
+// host on the engine's copy stream. Row r is atom r (checked on the device), so a row range is
+// an atom range of f.
+template <typename T>
+ljx_status force_to_host_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a,
+                              const ljx_list *l, int newton_pair, double scale, double *f_host,
+                              int pieces)
+{
+  const Modes m = decide_modes(e->c, newton_pair);
+  const bool lj = e->c.potential == LJX_POTENTIAL_LJ;
+  if (lj ? m.lj != ljx::kLjEdgeFull : m.force != ljx::kRowsFull)
+    return fail(e, LJX_ERR_UNSUPPORTED,
+                "force rows stream to the host only when each list row holds its atom's whole "
+                "force (full list, newton off)");
+  if (e->copy_stream == nullptr)
+    check(cudaStreamCreateWithFlags(&e->copy_stream, cudaStreamNonBlocking),
+          "cudaStreamCreateWithFlags(copy)");
+  for (cudaEvent_t &ev : e->piece_done)
+    if (ev == nullptr) check(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
+  ljx::Step<T> p = make_step<T>(e, a, l, scale);
+  set_pack_rules(p, e->c, m);
+  e->last_scale = scale;
+  const int inum = std::max(0, std::min(p.inum, a->nlocal));
+  check(cudaMemsetAsync(e->order_bad, 0, sizeof(int), s), "cudaMemsetAsync(order)");
+  if (inum > 0) {
+    k_rows_in_order<<<flat_grid(inum), ljx::kBlock, 0, s>>>(p.ilist, inum, e->order_bad);
+    check_launch("k_rows_in_order");
+    e->launches++;
+  }
+  check(cudaMemcpyAsync(e->host_order_bad, e->order_bad, sizeof(int), cudaMemcpyDeviceToHost, s),
+        "cudaMemcpyAsync(order)");
+  const int part = lj ? kLjPart : kForcePart;
+  double *partials = e->partial(part);
+  const int cap = e->max_grid / pieces;
+  const bool tally = p.eatom != nullptr || p.vatom != nullptr;
+  int blocks = 0;
+  for (int k = 0; k < pieces; ++k) {
+    const int r0 = static_cast<int>(static_cast<long long>(inum) * k / pieces);
+    const int r1 = static_cast<int>(static_cast<long long>(inum) * (k + 1) / pieces);
+    ljx::Step<T> q = p;
+    q.ilist = p.ilist + r0;
+    q.ccount = p.ccount + r0;
+    q.cedges = p.cedges + static_cast<long long>(r0) * p.row_cap;
+    q.inum = r1 - r0;
+    q.partials = partials + static_cast<long long>(blocks) * ljx::kPartialWidth;
+    if (q.inum > 0) {
+      if (lj) {
+        auto run = [&](auto kernel) {
+          const int grid = std::min(row_grid(e, q.inum, blocks_per_sm(kernel)), cap);
+          kernel<<<grid, ljx::kBlock, 0, s>>>(q);
+          return grid;
+        };
+        blocks += tally ? run(ljx::k_lj<T, ljx::kLjEdgeFull, true, true>)
+                        : run(ljx::k_lj<T, ljx::kLjEdgeFull, true, false>);
+        check_launch("k_lj");
+        e->launches++;
+        e->step_blocks[kLjPart] = blocks;
+      } else {
+        blocks += launch_force<T>(e, s, q, m.force, blocks, cap);
+      }
+    }
+    // Rows r0..r1-1 of f are final; the last piece also takes owned atoms without a list row.
+    const int c1 = k + 1 == pieces ? a->nlocal : r1;
+    check(cudaEventRecord(e->piece_done[k], s), "cudaEventRecord(piece)");
+    if (c1 > r0) {
+      check(cudaStreamWaitEvent(e->copy_stream, e->piece_done[k], 0), "cudaStreamWaitEvent(copy)");
+      check(cudaMemcpyAsync(f_host + 3LL * r0, a->f + 3LL * r0,
+                            3ULL * static_cast<size_t>(c1 - r0) * sizeof(double),
+                            cudaMemcpyDeviceToHost, e->copy_stream),
+            "cudaMemcpyAsync(f rows)");
+    }
+  }
+  if (lj) e->last_duplicate = m.duplicate ? 2 : 1;
+  check(cudaEventRecord(e->piece_done[16], e->copy_stream), "cudaEventRecord(copies)");
+  check(cudaStreamWaitEvent(s, e->piece_done[16], 0), "cudaStreamWaitEvent(stream)");
+  e->rows_streamed = true;
   return LJX_OK;
 }
 
@@ -799,7 +927,8 @@ ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **
     e->rows_cap = c.max_owned > 0 ? c.max_owned : c.max_atoms;
     e->row_cap = matrix ? c.max_neighbors
                         : static_cast<int>(std::max<long long>(1, c.max_edges / e->rows_cap));
-    e->max_grid = e->sm_count * 8;
+    // Room for a force pass launched in up to 16 pieces (ljx_force_to_host).
+    e->max_grid = e->sm_count * 64;
     e->xd4 = static_cast<double4 *>(device_alloc(max_atoms * sizeof(double4), "cudaMalloc(xd4)"));
     check(cudaMemset(e->xd4, 0, max_atoms * sizeof(double4)), "cudaMemset(xd4)");
     // Float copy of the positions: the distance pre-filter (and the float model) reads it.
@@ -863,6 +992,9 @@ ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **
     e->result = static_cast<double *>(device_alloc(16 * sizeof(double), "cudaMalloc(result)"));
     check(cudaMallocHost(reinterpret_cast<void **>(&e->host_result), 16 * sizeof(double)),
           "cudaMallocHost(result)");
+    e->order_bad = reinterpret_cast<int *>(e->result + 12);
+    e->host_order_bad = reinterpret_cast<int *>(e->host_result + 12);
+    *e->host_order_bad = 0;
     if (c.potential == LJX_POTENTIAL_EAM) {
       const ljx::EamTables &t = e->bundle.eam;
       // Slope rows (c1, 2 c2, 3 c3, 0) / dr: d rho/dr = s0 + t (s1 + t s2).
@@ -1010,6 +1142,51 @@ ljx_status ljx_force(ljx_engine *e, void *stream, const ljx_atoms *atoms, const 
   });
 }
 
+ljx_status ljx_force_only(ljx_engine *e, void *stream, const ljx_atoms *atoms,
+                          const ljx_list *list, int newton_pair, double scale)
+{
+  return guarded(e, [&]() -> ljx_status {
+    const ljx_status st = check_list(e, list);
+    if (st != LJX_OK) return st;
+    if (atoms == nullptr || atoms->f == nullptr)
+      return fail(e, LJX_ERR_INVALID, "force array is missing");
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? force_only_impl<double>(e, s, atoms, list, newton_pair, scale)
+                  : force_only_impl<float>(e, s, atoms, list, newton_pair, scale);
+  });
+}
+
+ljx_status ljx_force_to_host(ljx_engine *e, void *stream, const ljx_atoms *atoms,
+                             const ljx_list *list, int newton_pair, double scale, double *f_host,
+                             int pieces)
+{
+  return guarded(e, [&]() -> ljx_status {
+    const ljx_status st = check_list(e, list);
+    if (st != LJX_OK) return st;
+    if (atoms == nullptr || atoms->f == nullptr)
+      return fail(e, LJX_ERR_INVALID, "force array is missing");
+    if (f_host == nullptr || pieces < 1 || pieces > 16)
+      return fail(e, LJX_ERR_INVALID, "f_host is missing or pieces is outside 1..16");
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? force_to_host_impl<double>(e, s, atoms, list, newton_pair, scale, f_host, pieces)
+                  : force_to_host_impl<float>(e, s, atoms, list, newton_pair, scale, f_host,
+                                              pieces);
+  });
+}
+
+// After the stream has drained: a streamed force step whose rows were not in atom order.
+static ljx_status check_streamed_rows(ljx_engine *e)
+{
+  if (!e->rows_streamed) return LJX_OK;
+  e->rows_streamed = false;
+  if (*e->host_order_bad != 0)
+    return fail(e, LJX_ERR_INVALID,
+                "ljx_force_to_host: " + std::to_string(*e->host_order_bad) +
+                    " list rows are not their own atom (ilist[r] != r); the host force rows are "
+                    "not usable");
+  return LJX_OK;
+}
+
 ljx_status ljx_read_result(ljx_engine *e, void *stream, ljx_result *out)
 {
   return guarded(e, [&]() -> ljx_status {
@@ -1027,8 +1204,11 @@ ljx_status ljx_read_result(ljx_engine *e, void *stream, ljx_result *out)
     check(cudaStreamSynchronize(s), "cudaStreamSynchronize(result)");
     const double *r = e->host_result;
     ljx_result res{};
-    res.energy = r[0];
-    for (int k = 0; k < 6; ++k) res.virial[k] = r[1 + k];
+    if (e->step_ev) {
+      res.energy = r[0];
+      for (int k = 0; k < 6; ++k) res.virial[k] = r[1 + k];
+    }
+    e->step_ev = true;
     res.edge_count = static_cast<long long>(r[7]) * e->last_duplicate;
     res.widest_row = static_cast<int>(r[8]);
     if (e->c.input_layout == LJX_LAYOUT_NEIGHBOR_MATRIX)
@@ -1037,7 +1217,7 @@ ljx_status ljx_read_result(ljx_engine *e, void *stream, ljx_result *out)
       res.overflow = res.edge_count > e->c.max_edges;
     if (out) *out = res;
     for (int &b : e->step_blocks) b = 0;
-    return LJX_OK;
+    return check_streamed_rows(e);
   });
 }
 
@@ -1064,16 +1244,19 @@ ljx_status ljx_read_result_all(ljx_engine *e, ljx_halo *halo, void *stream, ljx_
     const ljx_status st = ljx::halo_reduce_fetch(halo, s, 8, 3, 12, r, why);
     if (st != LJX_OK) return fail(e, st, why);
     ljx_result_all res{};
-    res.energy = r[0];
-    for (int k = 0; k < 6; ++k) res.virial[k] = r[1 + k];
+    if (e->step_ev) {
+      res.energy = r[0];
+      for (int k = 0; k < 6; ++k) res.virial[k] = r[1 + k];
+    }
     res.edge_count = static_cast<long long>(r[7]);
     res.edge_max = static_cast<long long>(r[8]);
     res.widest_row = static_cast<int>(r[9]);
     res.overflow = r[10] > 0.0 ? 1 : 0;
-    res.local_energy = r[11];
+    res.local_energy = e->step_ev ? r[11] : 0.0;
+    e->step_ev = true;
     if (out) *out = res;
     for (int &b : e->step_blocks) b = 0;
-    return LJX_OK;
+    return check_streamed_rows(e);
   });
 }
 

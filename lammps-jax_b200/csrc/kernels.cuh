@@ -37,10 +37,15 @@ constexpr int kQueue = 64;
 #define LJX_DENSITY_BOUNDS __launch_bounds__(kBlock)
 #endif
 // The force pass: 4 blocks of 256 per SM (64 registers); the double half-list variant, which
-// spills at 64, runs 3 (80 registers) and is faster for it.
+// spills at 64, runs 3 (80 registers) and is faster for it. Force-only passes (no energy or
+// virial sums) hold 14 fewer registers per thread.
+#ifndef LJX_FORCE_ONLY_MIN_BLOCKS
+#define LJX_FORCE_ONLY_MIN_BLOCKS 4
+#endif
 #define LJX_FORCE_BOUNDS                                                                   \
   __launch_bounds__(kBlock, TALLY ? 2                                                       \
-                            : (sizeof(T) == 8 && MODE == kHalf) ? 3 : LJX_FORCE_MIN_BLOCKS)
+                            : (sizeof(T) == 8 && MODE == kHalf) ? 3                         \
+                            : !EV ? LJX_FORCE_ONLY_MIN_BLOCKS : LJX_FORCE_MIN_BLOCKS)
 
 enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2 };
 // Force distribution modes.
@@ -633,7 +638,8 @@ __global__ void __launch_bounds__(kBlock) k_embed(const Step<T> p)
 // phi and half of this edge's -rij (x) F_e into the row sums er / vr; the neighbor j takes the
 // other half of the energy when each pair appears once (half list) and the other half of the
 // virial when the force acts on j too (newton-on scatter), both by atomics into its rows.
-template <typename T, int MODE, bool FORCES = true, bool TALLY = false>
+// Without EV (force-only steps) neither the pair energy nor the virial is summed.
+template <typename T, int MODE, bool FORCES = true, bool TALLY = false, bool EV = true>
 __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T>::type &pi,
                                          int si, T fpi, int j, const typename Vec4<T>::type &pj,
                                          int sj, T fpj, T &fx, T &fy, T &fz, double &e,
@@ -651,7 +657,7 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   const auto c = load4_tab(p.pair + pair_row(si, sj) * p.nr + node);
   const T z2 = c.x + t * (c.y + t * (c.z + t * c.w));
   const T phi = z2 * rinv;
-  e += static_cast<double>(phi);
+  if constexpr (EV) e += static_cast<double>(phi);
   if constexpr (TALLY) {
     er += 0.5 * static_cast<double>(phi);
     if (MODE == kHalf && p.eatom != nullptr && j < p.nall)
@@ -679,8 +685,10 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
     const double c6[6] = {static_cast<double>(dx * ex), static_cast<double>(dy * ey),
                           static_cast<double>(dz * ez), static_cast<double>(dx * ey),
                           static_cast<double>(dx * ez), static_cast<double>(dy * ez)};
+    if constexpr (EV) {
 #pragma unroll
-    for (int k = 0; k < 6; ++k) v[k] += c6[k];
+      for (int k = 0; k < 6; ++k) v[k] += c6[k];
+    }
     if constexpr (TALLY) {
 #pragma unroll
       for (int k = 0; k < 6; ++k) vr[k] -= 0.5 * c6[k];
@@ -735,8 +743,9 @@ __device__ __forceinline__ typename Vec4<T>::type load_pos(const Step<T> &p, int
 
 // a9..a13: fused force + pair energy + virial over the compacted rows. Spilled rows (more kept
 // pairs than row_cap) re-walk the LAMMPS list with the same filter. Without FORCES: the pair
-// energy alone (energy-only evaluation; no F', no force or virial).
-template <typename T, int MODE, bool FORCES = true, bool TALLY = false>
+// energy alone (energy-only evaluation; no F', no force or virial). Without EV: the forces
+// alone (the steps where LAMMPS asks for neither energy nor virial); no partial sums are written.
+template <typename T, int MODE, bool FORCES = true, bool TALLY = false, bool EV = true>
 __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
 {
   using V = typename Vec4<T>::type;
@@ -787,7 +796,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
         for (int k = lane; k < n; k += kWarp) {
           const int j = load_once(crow + k);
           const V pj = load_pos(p, j);
-          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
+          eam_edge<T, MODE, FORCES, TALLY, EV>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
                                            kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
                                            er, vr);
         }
@@ -814,7 +823,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
             pj2 = load_pos(p, j2);
             if (kNeedFpj) fpj2 = __ldg(p.fp + j2);
           }
-          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w), fpj,
+          eam_edge<T, MODE, FORCES, TALLY, EV>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w), fpj,
                                            fx, fy, fz, e, v, er, vr);
           k = k2;
           j = j2;
@@ -831,7 +840,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
         if (j >= p.max_atoms) continue;
         if (pack_keep(p, i, xi, j, load4(p.xd4 + j))) {
           const V pj = load_pos(p, j);
-          eam_edge<T, MODE, FORCES, TALLY>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
+          eam_edge<T, MODE, FORCES, TALLY, EV>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
                                            kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
                                            er, vr);
         }
@@ -853,10 +862,13 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
   // Pair energy: phi/2 per directed edge of a full list, phi per edge of a half list. Virial:
   // -1/2 rij (x) F_e when every pair appears in two rows, -rij (x) F_e when the receiver takes
   // -F_e (newton-on scatters).
-  const double ew = MODE == kHalf ? 1.0 : 0.5;
-  const double vw = MODE == kRowsFull ? -0.5 : -1.0;
-  double acc[8] = {ew * e, vw * v[0], vw * v[1], vw * v[2], vw * v[3], vw * v[4], vw * v[5], 0.0};
-  store_partials(acc, 0, p.partials);
+  if constexpr (EV) {
+    const double ew = MODE == kHalf ? 1.0 : 0.5;
+    const double vw = MODE == kRowsFull ? -0.5 : -1.0;
+    double acc[8] = {ew * e, vw * v[0], vw * v[1], vw * v[2], vw * v[3], vw * v[4], vw * v[5],
+                     0.0};
+    store_partials(acc, 0, p.partials);
+  }
 }
 
 // LJ 12-6 in one pass over the LAMMPS list: examples/export_model.py:16-74 with the force-add

@@ -108,9 +108,15 @@ __global__ void k_bin_order(const int *__restrict__ start, long long nb, int *bi
 // broadcasts). Kept neighbors append to the rows in shared memory in stencil order; slots past
 // kRowCap go straight to global memory. The rows then leave slot-major, so one store covers the
 // same slot of consecutive rows (LayoutLeft).
+#ifndef LJX_NEIGH_ROW_CAP
+#define LJX_NEIGH_ROW_CAP 256
+#endif
+#ifndef LJX_NEIGH_WARPS
+#define LJX_NEIGH_WARPS 4
+#endif
 constexpr int kRowsPerPass = 8;
-constexpr int kRowCap = 256;
-constexpr int kNeighWarps = 4;
+constexpr int kRowCap = LJX_NEIGH_ROW_CAP;
+constexpr int kNeighWarps = LJX_NEIGH_WARPS;
 
 __global__ void __launch_bounds__(kNeighWarps * 32)
 k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, Grid g,

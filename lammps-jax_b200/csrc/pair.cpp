@@ -303,7 +303,12 @@ ljx_status ljx_pair_compute(ljx_pair *pair, void *stream, const ljx_atoms *atoms
         return pair->fail(LJX_ERR_CUDA, "LAMMPS-JAX compute failed: forward comm of F' failed");
     }
     if (atoms->f == nullptr) return pair->fail(LJX_ERR_INVALID, "force array is missing");
-    if (ljx_force(e, stream, atoms, list, newton_pair, pair->scale) != LJX_OK)
+    // Steps without energy or virial requests (all but thermo steps) run the forces alone, as
+    // the reference runs its force program (:1055-1057).
+    const bool ev = (flags & (LJX_EFLAG_GLOBAL | LJX_VFLAG_GLOBAL | LJX_EFLAG_ATOM |
+                              LJX_VFLAG_ATOM)) != 0;
+    if ((ev ? ljx_force(e, stream, atoms, list, newton_pair, pair->scale)
+            : ljx_force_only(e, stream, atoms, list, newton_pair, pair->scale)) != LJX_OK)
       return compute_failed();
   }
   ljx_result res{};

@@ -167,6 +167,24 @@ class Engine:
         self._check(self.lib.ljx_force(self._h, _stream(stream), ctypes.byref(atoms),
                                        ctypes.byref(nl), int(newton_pair), float(scale)))
 
+    def force_only(self, atoms, nl, newton_pair, scale=1.0, stream=None):
+        """The forces without the energy and virial sums (steps where LAMMPS asks for
+        neither); the next read_result reports energy and virial as zero."""
+        self._check(self.lib.ljx_force_only(self._h, _stream(stream), ctypes.byref(atoms),
+                                            ctypes.byref(nl), int(newton_pair), float(scale)))
+
+    def force_to_host(self, atoms, nl, newton_pair, f_host, scale=1.0, pieces=4, stream=None):
+        """ljx_force with the owned force rows copied into `f_host` (a pinned CPU float64
+        tensor of nlocal x 3) piece by piece while the pass runs; complete once the stream has
+        drained (read_result)."""
+        if f_host.device.type != "cpu" or f_host.dtype != torch.float64 or not f_host.is_contiguous():
+            raise ValueError("f_host must be a contiguous float64 CPU tensor")
+        if f_host.numel() < 3 * atoms.nlocal:
+            raise ValueError("f_host holds fewer than nlocal rows")
+        self._check(self.lib.ljx_force_to_host(self._h, _stream(stream), ctypes.byref(atoms),
+                                               ctypes.byref(nl), int(newton_pair), float(scale),
+                                               ctypes.c_void_p(f_host.data_ptr()), int(pieces)))
+
     def energy(self, atoms, nl, newton_pair, scale=1.0, stream=None):
         self._check(self.lib.ljx_energy(self._h, _stream(stream), ctypes.byref(atoms),
                                         ctypes.byref(nl), int(newton_pair), float(scale)))
