@@ -7,7 +7,8 @@
 // signal the reference's neighbor-matrix path also follows, cpp/pair_jax_kokkos.cpp:1011-1012),
 // k_build_groups stores for each group of kGroupRows consecutive rows:
 //   - the union of the rows' neighbors within rc + margin (about 300 atoms for 8 rows at C3);
-//   - for each row, its candidates within rc + margin as 16-bit slots into that union.
+//   - for each row, its candidates within rc + margin as 16-bit slots into that union, in the
+//     order of the row's LAMMPS list (so the kept pairs come out as the list pass emits them).
 // Every step, k_density_groups runs one block per group. The block stages the union's positions
 // in shared memory (one global gather per union atom, shared by the eight rows). Then, as in the
 // list pass, one warp per row filters its candidates with the reference's exact keep test,
@@ -50,31 +51,35 @@ static_assert(kUnionMax < kHashSlots, "the set must keep free slots");
 // decision is uniform over the grid. Also records the positions the displacement is measured
 // from. cand_cutsq is (rc + margin)^2; the float test uses its rounding band, so a pair whose
 // exact distance is within rc + margin is never dropped.
+//
+// One warp per group. Lane l walks row l % 8, four list slots per step (with LayoutLeft and
+// consecutive rows, one step reads slot s of all eight rows as one 32-byte sector). Each
+// candidate is looked up in the warp's hash set (a plain read first: most candidates of a group
+// are already there, about 3.6 rows share each neighbor) and inserted by compare-and-swap when
+// absent; a new atom takes the next union index, in first-seen order, and is written out at
+// once. Every candidate then goes straight into its row's slot list as its union index, so a
+// row's candidates keep the order of its LAMMPS list.
 template <typename T>
 __global__ void __launch_bounds__(kBuildBlock)
 k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, double cand_cutsq)
 {
-  __shared__ int s_key[kBuildWarps][kHashSlots];
-  __shared__ unsigned s_mask[kBuildWarps][kHashSlots / 4];
-  __shared__ unsigned short s_used[kBuildWarps][kUnionMax];
+  __shared__ __align__(16) int s_key[kBuildWarps][kHashSlots];
+  __shared__ unsigned short s_index[kBuildWarps][kHashSlots];
   if (!force_build && !(__uint_as_float(*p.disp_bound) > disp_limit)) return;
   for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < span; a += gridDim.x * blockDim.x)
     p.xref[a] = p.xd4[a];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
-  int *key = s_key[warp];
-  unsigned *mask = s_mask[warp];
-  unsigned short *used = s_used[warp];
+  volatile int *key = s_key[warp];
+  unsigned short *uindex = s_index[warp];
+  int4 *key4 = reinterpret_cast<int4 *>(s_key[warp]);
   const float4 *pos4f = reinterpret_cast<const float4 *>(p.pos4);
   const FilterBand band = filter_band(cand_cutsq, *p.coord_bound);
   const int groups = (p.inum + kGroupRows - 1) / kGroupRows;
-  // The set starts empty once; each group then empties only the slots it used.
-  for (int h = lane; h < kHashSlots; h += kWarp) key[h] = -1;
-  for (int h = lane; h < kHashSlots / 4; h += kWarp) mask[h] = 0u;
+  // The set starts empty; each group empties it again when done.
+  for (int h = lane; h < kHashSlots / 4; h += kWarp) key4[h] = make_int4(-1, -1, -1, -1);
   __syncwarp();
   for (int g = blockIdx.x * kBuildWarps + warp; g < groups; g += gridDim.x * kBuildWarps) {
-    // Lane l walks row l % 8, four slots per step: with LayoutLeft and consecutive rows, one
-    // step reads slot s of all eight rows as one 32-byte sector.
     const int k = lane & (kGroupRows - 1);
     const int row = g * kGroupRows + k;
     int i = -1, n = 0;
@@ -91,10 +96,13 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
     int longest = n;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) longest = max(longest, __shfl_xor_sync(kFull, longest, o));
+    const unsigned rowlanes = 0x01010101u << k;  // the four lanes of this lane's row
+    unsigned short *slots = p.rslot + static_cast<long long>(row) * p.rcap;
+    int *out = p.gatom + static_cast<long long>(g) * p.gcap;
     bool lost = false;
     int total = 0;  // distinct atoms so far (uniform over the warp)
+    int got = 0;    // candidates of this lane's row so far (uniform over the row's lanes)
     const long long rowbase = static_cast<long long>(i) * p.atom_stride;
-    const unsigned bit = 1u << static_cast<unsigned>(k);
     for (int s0 = 0; s0 < longest; s0 += kWarp / kGroupRows) {
       const int s = s0 + lane / kGroupRows;
       bool cand = false;
@@ -107,17 +115,15 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
           cand = dx * dx + dy * dy + dz * dz <= band.hi;
         }
       }
-      // Insert j (multiplicative hash, linear probing). The lane that places a new atom
-      // records its slot; the union keeps that first-seen order, which is the order of the
-      // LAMMPS rows' own lists.
+      // Multiplicative hash, linear probing.
       unsigned h = (static_cast<unsigned>(j) * 0x9E3779B1u) >> 22;
       bool fresh = false;
       if (cand) {
         bool placed = false;
         for (int probe = 0; probe < kHashSlots; ++probe) {
-          const int cur = atomicCAS(key + h, -1, j);
+          int cur = key[h];
+          if (cur == -1) cur = atomicCAS(const_cast<int *>(key) + h, -1, j);
           if (cur == -1 || cur == j) {
-            atomicOr(mask + (h >> 2), bit << ((h & 3u) * 8u));
             fresh = cur == -1;
             placed = true;
             break;
@@ -126,61 +132,30 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
         }
         lost |= !placed;
       }
-      const unsigned m = __ballot_sync(kFull, fresh);
+      const unsigned fm = __ballot_sync(kFull, fresh);
       if (fresh) {
-        const int at = total + __popc(m & below);
-        if (at < kUnionMax) used[at] = static_cast<unsigned short>(h);
+        const int at = total + __popc(fm & below);
+        uindex[h] = static_cast<unsigned short>(min(at, 65535));
+        if (at < p.gcap) out[at] = j;
       }
-      total += __popc(m);
-    }
-    lost = __any_sync(kFull, lost) || total > kUnionMax;
-    __syncwarp();
-    // Union in first-seen order, then each row's candidates as slots into it (union order).
-    const int stored = min(total, kUnionMax);
-    bool spilled = lost || total > p.gcap;
-    if (!spilled) {
-      int *out = p.gatom + static_cast<long long>(g) * p.gcap;
-      for (int at = lane; at < stored; at += kWarp) out[at] = key[used[at]];
-      for (int r = 0; r < kGroupRows && !spilled; ++r) {
-        const int rrow = g * kGroupRows + r;
-        if (rrow >= p.inum) break;
-        unsigned short *slots = p.rslot + static_cast<long long>(rrow) * p.rcap;
-        int got = 0;
-        for (int base = 0; base < stored; base += kWarp) {
-          const int at = base + lane;
-          bool has = false;
-          if (at < stored) {
-            const int h = used[at];
-            has = (mask[h >> 2] >> ((h & 3) * 8 + r)) & 1u;
-          }
-          const unsigned m = __ballot_sync(kFull, has);
-          if (has) {
-            const int pos = got + __popc(m & below);
-            if (pos < p.rcap) slots[pos] = static_cast<unsigned short>(at);
-          }
-          got += __popc(m);
-        }
-        if (lane == 0) p.rcount[rrow] = got;
-        spilled = got > p.rcap;
+      total += __popc(fm);
+      __syncwarp();  // the new atoms' union indices are visible to every lane
+      const unsigned cm = __ballot_sync(kFull, cand);
+      if (cand) {
+        const int at = got + __popc(cm & rowlanes & below);
+        if (at < p.rcap) slots[at] = uindex[h];
       }
+      got += __popc(cm & rowlanes);
     }
-    __syncwarp();
-    // Empty the used slots for the next group (the whole set if not every slot was recorded).
-    if (total > kUnionMax) {
-      for (int h = lane; h < kHashSlots; h += kWarp) key[h] = -1;
-      for (int h = lane; h < kHashSlots / 4; h += kWarp) mask[h] = 0u;
-    } else {
-      for (int at = lane; at < stored; at += kWarp) {
-        const int h = used[at];
-        key[h] = -1;
-        mask[h >> 2] = 0u;
-      }
-    }
-    __syncwarp();
     // A group that does not fit is marked past capacity; the density pass then walks its rows'
     // lists instead.
-    if (lane == 0) p.gcount[g] = spilled ? p.gcap + 1 : total;
+    const bool spilled = __any_sync(kFull, lost || got > p.rcap) || total > kUnionMax ||
+                         total > p.gcap;
+    if (lane < kGroupRows && row < p.inum) p.rcount[row] = got;
     __syncwarp();
+    for (int h = lane; h < kHashSlots / 4; h += kWarp) key4[h] = make_int4(-1, -1, -1, -1);
+    __syncwarp();
+    if (lane == 0) p.gcount[g] = spilled ? p.gcap + 1 : total;
   }
 }
 

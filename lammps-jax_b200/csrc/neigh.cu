@@ -108,8 +108,11 @@ __global__ void k_bin_order(const int *__restrict__ start, long long nb, int *bi
 // broadcasts). Kept neighbors append to the rows in shared memory in stencil order; slots past
 // kRowCap go straight to global memory. The rows then leave slot-major, so one store covers the
 // same slot of consecutive rows (LayoutLeft).
+// Row staging capacity: 192 slots (24 KB per 4-warp block) measured faster than 256 (32 KB) at
+// 214 and 261 neighbors per row (C3, C5), by more resident blocks; the slots past it go
+// straight to global memory. 128 was slower again.
 #ifndef LJX_NEIGH_ROW_CAP
-#define LJX_NEIGH_ROW_CAP 256
+#define LJX_NEIGH_ROW_CAP 192
 #endif
 #ifndef LJX_NEIGH_WARPS
 #define LJX_NEIGH_WARPS 4
@@ -188,26 +191,28 @@ k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, G
       s_start[warp][lane] = start;
       s_off[warp][lane] = incl - len;
       __syncwarp();
-      for (int s0 = 0; s0 < total; s0 += 32) {
-        int j = -1;
-        double xj = 0, yj = 0, zj = 0;
-        const int k = s0 + lane;
+      // Candidate k's stencil row is the last row whose offset is <= k (empty rows share their
+      // offset with the next one, so they are never the last). A lane's k grows by 32 per
+      // batch, about one row, so the row only moves forward; the next batch's atom and position
+      // are fetched before this batch's tests, so their latency overlaps them.
+      int q = 0;
+      auto fetch = [&](int k, int &j, double &xa, double &ya, double &za) {
+        j = -1;
         if (k < total) {
-          // The stencil row holding candidate k: the last row whose offset is <= k (empty
-          // rows share their offset with the next one, so they are never the last).
-          int lo = 0, hi = 24;
-          while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (s_off[warp][mid] <= k)
-              lo = mid;
-            else
-              hi = mid - 1;
-          }
-          j = bin_atoms[s_start[warp][lo] + (k - s_off[warp][lo])];
-          xj = x[3 * j];
-          yj = x[3 * j + 1];
-          zj = x[3 * j + 2];
+          while (q < 24 && s_off[warp][q + 1] <= k) ++q;
+          j = bin_atoms[s_start[warp][q] + (k - s_off[warp][q])];
+          xa = x[3 * j];
+          ya = x[3 * j + 1];
+          za = x[3 * j + 2];
         }
+      };
+      int jn = -1;
+      double xn = 0, yn = 0, zn = 0;
+      fetch(lane, jn, xn, yn, zn);
+      for (int s0 = 0; s0 < total; s0 += 32) {
+        const int j = jn;
+        const double xj = xn, yj = yn, zj = zn;
+        fetch(s0 + 32 + lane, jn, xn, yn, zn);
 #pragma unroll
         for (int r = 0; r < kRowsPerPass; ++r) {
           if (r >= m) continue;  // m is the same for every lane
