@@ -408,9 +408,14 @@ def run_ljx(args):
     # The engine caches candidates only for lists that live at least 4 steps (kCacheMinPeriod in
     # csrc/engine.cu); shorter-lived lists take the list pass.
     cached = args.rebuild_every >= 4
-    kname = {"density": (f"k_density_groups_full_{precision}" if cached
-                         else f"k_density_full_{precision}"),
-             "force": f"k_force_rows_full_{precision}"}[kernel]
+    # EAM full lists with newton off hold each owned pair once unless LJX_OWNED_HALF=0
+    # (kDensityHalfOwned / kRowsHalfOwned in csrc/kernels.cuh).
+    owned = (not system.newton_pair and not system.list.half and
+             os.environ.get("LJX_OWNED_HALF", "1") != "0")
+    rows = "owned" if owned else "full"
+    kname = {"density": (f"k_density_groups_{rows}_{precision}" if cached
+                         else f"k_density_{rows}_{precision}"),
+             "force": f"k_force_rows_{rows}_{precision}"}[kernel]
     # DRAM bytes and L1 utilisation of this kernel come from committed one-kernel ncu captures
     # (C3 kernels by name, C5 ones as "c5:<name>"), labelled as such: no profiler runs here.
     key = {"c3": kname, "c5": f"c5:{kname}"}.get(args.config)

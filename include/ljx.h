@@ -181,7 +181,14 @@ ljx_status ljx_edges(ljx_engine *engine, const int **senders, const int **receiv
 /* a2+a6 — fused pass over the LAMMPS list: distance-filter and compact each row (warp ballot
  * compaction, rows kept in engine scratch) and accumulate the EAM density rho_i += f_j(r)
  * (python/lammps_jax/eam.py:284-314). For half lists the neighbor share is scattered too.
- * For LJ bundles it only compacts. */
+ * For LJ bundles it only compacts.
+ * EAM full lists with newton off hold each owned pair once: row i keeps the owned neighbors
+ * j > i and every ghost, and the neighbor's density share (here) and force (ljx_force) are added
+ * by atomics; the kept pairs, the edge count and all results are the reference's, with sums in
+ * an order that can differ between runs in the last bits. The environment variable
+ * LJX_OWNED_HALF=0, read by ljx_engine_create, evaluates every pair from both rows instead
+ * (bitwise reproducible, slower). Per-atom tallies and lists without a row for every owned atom
+ * use both rows too. */
 ljx_status ljx_density(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
                        const ljx_list *list, int newton_pair);
 

@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -160,6 +161,8 @@ struct ljx_engine {
   int *host_order_bad = nullptr;  // pinned: its copy (host_result slot 12)
   bool rows_streamed = false;
   bool step_ev = true;            // false after ljx_force_only: the result has no energy/virial
+  bool owned_half = true;         // allow owned pairs held once (LJX_OWNED_HALF, default on)
+  bool rows_owned_half = false;   // the last ljx_density compacted rows that hold them once
   std::string error;
 
   ~ljx_engine()
@@ -252,6 +255,7 @@ struct Modes {
   bool reverse_density = false;
   bool reverse_force = false;
   bool duplicate = false;
+  bool owned_half = false;  // owned pairs held once (kDensityHalfOwned / kRowsHalfOwned)
 };
 
 Modes decide_modes(const ljx_contract &c, int newton_pair)
@@ -290,6 +294,35 @@ Modes decide_modes(const ljx_contract &c, int newton_pair)
     else
       m.lj = m.half_list ? ljx::kLjAtomHalfPairSum : ljx::kLjAtomFull;
     m.reverse_force = newton_pair != 0;
+  }
+  return m;
+}
+
+// The modes a step runs with. EAM full lists with newton off hold each owned pair once
+// (kDensityHalfOwned / kRowsHalfOwned) unless the bundle has its own pairing rule, per-atom
+// tallies are registered, some owned atom has no list row (an owned pair must be held by the row
+// of its lower atom), or LJX_OWNED_HALF=0. ljx_density decides and records it; the force and
+// energy passes of the step follow the compacted rows it wrote.
+Modes density_modes(ljx_engine *e, int newton_pair, int inum, int nlocal)
+{
+  Modes m = decide_modes(e->c, newton_pair);
+  if (e->owned_half && e->c.potential == LJX_POTENTIAL_EAM && m.force == ljx::kRowsFull &&
+      !e->c.half_edges && e->eatom == nullptr && e->vatom == nullptr && inum == nlocal) {
+    m.owned_half = true;
+    m.density = ljx::kDensityHalfOwned;
+    m.force = ljx::kRowsHalfOwned;
+  }
+  e->rows_owned_half = m.owned_half;
+  return m;
+}
+
+Modes pass_modes(const ljx_engine *e, int newton_pair)
+{
+  Modes m = decide_modes(e->c, newton_pair);
+  if (e->rows_owned_half && m.force == ljx::kRowsFull) {
+    m.owned_half = true;
+    m.density = ljx::kDensityHalfOwned;
+    m.force = ljx::kRowsHalfOwned;
   }
   return m;
 }
@@ -361,7 +394,8 @@ template <typename T>
 void set_pack_rules(ljx::Step<T> &p, const ljx_contract &c, const Modes &m)
 {
   const bool full_list = !m.half_list;
-  p.half_rule = c.half_edges && full_list;
+  // Owned pairs held once keep the owned neighbors j > i and every ghost: the half rule's filter.
+  p.half_rule = (c.half_edges && full_list) || m.owned_half;
   p.unique_rule = c.half_edges && c.n_comm_widths > 0 && full_list;
 }
 
@@ -419,6 +453,10 @@ void launch_density(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
       grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_density<T, ljx::kDensityHalf>));
       ljx::k_density<T, ljx::kDensityHalf><<<grid, ljx::kBlock, 0, s>>>(p);
       break;
+    case ljx::kDensityHalfOwned:
+      grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_density<T, ljx::kDensityHalfOwned>));
+      ljx::k_density<T, ljx::kDensityHalfOwned><<<grid, ljx::kBlock, 0, s>>>(p);
+      break;
     case ljx::kCompactOnly:
       grid = row_grid(e, p.inum, blocks_per_sm(ljx::k_density<T, ljx::kCompactOnly>));
       ljx::k_density<T, ljx::kCompactOnly><<<grid, ljx::kBlock, 0, s>>>(p);
@@ -464,7 +502,8 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   e->groups_valid = true;
   e->groups_key = key;
   const int need = groups;  // one block per group
-  const bool rules = p.half_rule || p.unique_rule;
+  // The build applied the owned-pairs half rule already; other rules are re-checked each step.
+  const bool rules = (p.half_rule && mode != ljx::kDensityHalfOwned) || p.unique_rule;
   auto run = [&](auto kernel) {
     const int grid = std::max(1, std::min(need, std::min(e->max_grid,
                                                          e->sm_count * blocks_per_sm(kernel))));
@@ -475,6 +514,8 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   if (mode == ljx::kDensityHalf)
     grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityHalf, true>)
                  : run(ljx::k_density_groups<T, ljx::kDensityHalf, false>);
+  else if (mode == ljx::kDensityHalfOwned)
+    grid = run(ljx::k_density_groups<T, ljx::kDensityHalfOwned, false>);
   else
     grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityFull, true>)
                  : run(ljx::k_density_groups<T, ljx::kDensityFull, false>);
@@ -500,6 +541,10 @@ int launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
   switch (mode) {
     case ljx::kGhost: grid = run(ljx::k_force<T, ljx::kGhost, FORCES, TALLY, EV>); break;
     case ljx::kHalf: grid = run(ljx::k_force<T, ljx::kHalf, FORCES, TALLY, EV>); break;
+    case ljx::kRowsHalfOwned:
+      // Never with per-atom tallies: the density pass then keeps full rows.
+      if constexpr (!TALLY) grid = run(ljx::k_force<T, ljx::kRowsHalfOwned, FORCES, false, EV>);
+      break;
     default: grid = run(ljx::k_force<T, ljx::kRowsFull, FORCES, TALLY, EV>);
   }
   check_launch("k_force");
@@ -593,7 +638,7 @@ template <typename T>
 ljx_status density_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
                         int newton_pair)
 {
-  const Modes m = decide_modes(e->c, newton_pair);
+  const Modes m = density_modes(e, newton_pair, l ? l->inum : 0, a ? a->nlocal : 0);
   if (e->c.potential == LJX_POTENTIAL_LJ) return LJX_OK;  // LJ is one pass (ljx_force)
   ljx::Step<T> p = make_step<T>(e, a, l, 1.0);
   set_pack_rules(p, e->c, m);
@@ -602,6 +647,11 @@ ljx_status density_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const
     // Half lists scatter into neighbor rows, ghosts included: start from zero.
     const long long rows = std::min<long long>(p.nall, e->c.max_atoms);
     check(cudaMemsetAsync(e->rho, 0, rows * sizeof(T), s), "cudaMemsetAsync(rho)");
+  } else if ((m.density == ljx::kDensityHalfOwned || p.inum < p.nlocal) && p.nlocal > 0) {
+    // Owned pairs held once scatter into owned rows only; owned atoms without a list row have
+    // no density term (the reference's segment sum over their edges is empty).
+    check(cudaMemsetAsync(e->rho, 0, static_cast<long long>(p.nlocal) * sizeof(T), s),
+          "cudaMemsetAsync(rho)");
   }
   // Candidate cache policy. A build costs about as much as one list pass plus a third, and each
   // later step over the cache saves about a quarter of a list pass (C3), so a list has to live
@@ -646,7 +696,7 @@ template <typename T>
 ljx_status force_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
                       int newton_pair, double scale)
 {
-  const Modes m = decide_modes(e->c, newton_pair);
+  const Modes m = pass_modes(e, newton_pair);
   ljx::Step<T> p = make_step<T>(e, a, l, scale);
   set_pack_rules(p, e->c, m);
   e->last_scale = scale;
@@ -673,7 +723,7 @@ ljx_status force_only_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, co
     e->step_ev = false;
     return st;
   }
-  const Modes m = decide_modes(e->c, newton_pair);
+  const Modes m = pass_modes(e, newton_pair);
   ljx::Step<T> p = make_step<T>(e, a, l, scale);
   set_pack_rules(p, e->c, m);
   e->last_scale = scale;
@@ -701,9 +751,12 @@ ljx_status force_to_host_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a,
                               const ljx_list *l, int newton_pair, double scale, double *f_host,
                               int pieces)
 {
-  const Modes m = decide_modes(e->c, newton_pair);
+  const Modes m = pass_modes(e, newton_pair);
   const bool lj = e->c.potential == LJX_POTENTIAL_LJ;
-  if (lj ? m.lj != ljx::kLjEdgeFull : m.force != ljx::kRowsFull)
+  // Owned pairs held once scatter only into rows of higher index (j > i), so after each piece
+  // every row before its end is final too.
+  if (lj ? m.lj != ljx::kLjEdgeFull
+         : (m.force != ljx::kRowsFull && m.force != ljx::kRowsHalfOwned))
     return fail(e, LJX_ERR_UNSUPPORTED,
                 "force rows stream to the host only when each list row holds its atom's whole "
                 "force (full list, newton off)");
@@ -780,7 +833,7 @@ template <typename T>
 ljx_status energy_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
                        int newton_pair, double scale)
 {
-  const Modes m = decide_modes(e->c, newton_pair);
+  const Modes m = pass_modes(e, newton_pair);
   ljx::Step<T> p = make_step<T>(e, a, l, scale);
   set_pack_rules(p, e->c, m);
   e->last_scale = scale;
@@ -918,6 +971,7 @@ ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **
   }
   try {
     DeviceGuard guard(device);
+    if (const char *v = std::getenv("LJX_OWNED_HALF")) e->owned_half = std::atoi(v) != 0;
     check(cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, device),
           "cudaDeviceGetAttribute");
     e->f64 = c.precision == LJX_FLOAT64;

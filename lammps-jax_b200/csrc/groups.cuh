@@ -227,6 +227,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
       int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
       T rho = T(0);
       int kept = 0;
+      int kept_twice = 0;  // owned pairs held once (kDensityHalfOwned) count for both directions
       if (cached) {
         // About 80 % of a row's cached candidates are kept, so each batch of 32 evaluates its
         // kept pairs in place: the idle lanes cost little (a gather costs per sector touched,
@@ -267,10 +268,12 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
               const T r = pair_distance(r2);
               const int sj = static_cast<int>(xj.w);
               rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
-              if (MODE == kDensityHalf)
+              if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
                 atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
             }
           }
+          if (MODE == kDensityHalfOwned)
+            kept_twice += __popc(__ballot_sync(kFull, keep && j < p.nlocal));
           kept += __popc(m);
         }
       } else {
@@ -304,22 +307,24 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
             if (r2 < p.model_cutsq) {
               const T r = pair_distance(r2);
               rho += spline_v<T>(p.density + static_cast<int>(xj.w) * p.nr, p.nr, r, p.inv_dr);
-              if (MODE == kDensityHalf)
+              if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
                 atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
             }
           }
+          if (MODE == kDensityHalfOwned)
+            kept_twice += __popc(__ballot_sync(kFull, keep && j < p.nlocal));
           kept += __popc(m);
         }
       }
       rho = warp_sum(rho);
       if (lane == 0) {
-        if (MODE == kDensityHalf)
+        if (MODE == kDensityHalf || MODE == kDensityHalfOwned)
           atomicAdd(p.rho + i, rho);
         else
           p.rho[i] = rho;
         p.ccount[row] = kept;
       }
-      kept_sum += kept;
+      kept_sum += kept + kept_twice;
     }
     __syncthreads();
   }

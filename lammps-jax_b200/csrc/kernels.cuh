@@ -47,13 +47,20 @@ constexpr int kQueue = 64;
                             : (sizeof(T) == 8 && MODE == kHalf) ? 3                         \
                             : !EV ? LJX_FORCE_ONLY_MIN_BLOCKS : LJX_FORCE_MIN_BLOCKS)
 
-enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2 };
+// Density modes. kDensityHalfOwned: a full list with newton off whose rows keep only owned
+// neighbors j > i and all ghosts (the filter's half rule); each owned pair is evaluated once and
+// its share added to both rows, ghost pairs (also listed from the image's owner) to row i alone.
+enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2, kDensityHalfOwned = 3 };
 // Force distribution modes.
-//  kRowsFull : full list, newton off; row i takes the whole pair force, no scatter.
-//  kGhost    : full list, newton on, plain bundle; each edge carries F'(rho_i) rho_j' + phi'/2
-//              to both endpoints (the autodiff of the plain energy program).
-//  kHalf     : half list, newton on; whole pair force, sender +, receiver -.
-enum ForceMode { kRowsFull = 0, kGhost = 1, kHalf = 2 };
+//  kRowsFull       : full list, newton off; row i takes the whole pair force, no scatter.
+//  kGhost          : full list, newton on, plain bundle; each edge carries F'(rho_i) rho_j' +
+//                    phi'/2 to both endpoints (the autodiff of the plain energy program).
+//  kHalf           : half list, newton on; whole pair force, sender +, receiver -.
+//  kRowsHalfOwned  : the rows of kDensityHalfOwned; an owned pair's force goes to both atoms
+//                    (Newton's third law; the neighbor's share by atomics) and its energy and
+//                    virial count for both directions, a ghost pair's to row i alone. The same
+//                    pairs, forces, energy and virial as kRowsFull, from about half the pairs.
+enum ForceMode { kRowsFull = 0, kGhost = 1, kHalf = 2, kRowsHalfOwned = 3 };
 enum LjMode { kLjEdgeFull = 0, kLjEdgeHalf = 1, kLjAtomFull = 2, kLjAtomHalfPairSum = 3 };
 
 template <typename T> struct Vec4;
@@ -483,6 +490,7 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
       const long long rowbase = static_cast<long long>(i) * p.atom_stride;
       T rho = T(0);
       int kept = 0;  // pairs already written out
+      int kept_twice = 0;
       int q = 0;     // pairs waiting in the queue
       // Write out kept pair (i -> j) at `slot` of the compacted row and add its density.
       auto evaluate = [&](int slot, int j, float r2f) {
@@ -504,7 +512,7 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           if (r2 < p.model_cutsq) {
             const T r = pair_distance(r2);
             rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
-            if (MODE == kDensityHalf)
+            if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
               atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
           }
         }
@@ -559,6 +567,8 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           }
         }
         const unsigned m = __ballot_sync(kFull, keep);
+        // Owned pairs held once stand for both directions in the kept-edge count.
+        if (MODE == kDensityHalfOwned) kept_twice += __popc(__ballot_sync(kFull, keep && j < p.nlocal));
         if constexpr (sizeof(T) == 4) {
           // Float runs evaluate kept pairs in place: their evaluation gathers only the species
           // word, so idle lanes cost less than the queue's shared-memory round trip.
@@ -580,14 +590,14 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
       if (MODE != kCompactOnly) {
         rho = warp_sum(rho);
         if (lane == 0) {
-          if (MODE == kDensityHalf)
+          if (MODE == kDensityHalf || MODE == kDensityHalfOwned)
             atomicAdd(p.rho + i, rho);
           else
             p.rho[i] = rho;
         }
       }
       if (lane == 0) p.ccount[row] = kept;
-      kept_sum += kept;
+      kept_sum += kept + kept_twice;
     }
     __syncthreads();
   }
@@ -657,7 +667,9 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
   const auto c = load4_tab(p.pair + pair_row(si, sj) * p.nr + node);
   const T z2 = c.x + t * (c.y + t * (c.z + t * c.w));
   const T phi = z2 * rinv;
-  if constexpr (EV) e += static_cast<double>(phi);
+  // An owned pair held once (kRowsHalfOwned) counts for both directions.
+  const bool twice = MODE == kRowsHalfOwned && j < p.nlocal;
+  if constexpr (EV) e += twice ? 2.0 * static_cast<double>(phi) : static_cast<double>(phi);
   if constexpr (TALLY) {
     er += 0.5 * static_cast<double>(phi);
     if (MODE == kHalf && p.eatom != nullptr && j < p.nall)
@@ -687,16 +699,16 @@ __device__ __forceinline__ void eam_edge(const Step<T> &p, const typename Vec4<T
                           static_cast<double>(dx * ez), static_cast<double>(dy * ez)};
     if constexpr (EV) {
 #pragma unroll
-      for (int k = 0; k < 6; ++k) v[k] += c6[k];
+      for (int k = 0; k < 6; ++k) v[k] += twice ? 2.0 * c6[k] : c6[k];
     }
     if constexpr (TALLY) {
 #pragma unroll
       for (int k = 0; k < 6; ++k) vr[k] -= 0.5 * c6[k];
-      if (MODE != kRowsFull && p.vatom != nullptr && j < p.nall)
+      if ((MODE == kGhost || MODE == kHalf) && p.vatom != nullptr && j < p.nall)
 #pragma unroll
         for (int k = 0; k < 6; ++k) atomicAdd(p.vatom + 6 * j + k, -0.5 * p.tally_scale * c6[k]);
     }
-    if (MODE != kRowsFull && j < p.nall) {
+    if (((MODE == kGhost || MODE == kHalf) && j < p.nall) || twice) {
       atomicAdd(p.f + 3 * j + 0, -p.scale * static_cast<double>(ex));
       atomicAdd(p.f + 3 * j + 1, -p.scale * static_cast<double>(ey));
       atomicAdd(p.f + 3 * j + 2, -p.scale * static_cast<double>(ez));
@@ -864,7 +876,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
   // -F_e (newton-on scatters).
   if constexpr (EV) {
     const double ew = MODE == kHalf ? 1.0 : 0.5;
-    const double vw = MODE == kRowsFull ? -0.5 : -1.0;
+    const double vw = (MODE == kRowsFull || MODE == kRowsHalfOwned) ? -0.5 : -1.0;
     double acc[8] = {ew * e, vw * v[0], vw * v[1], vw * v[2], vw * v[3], vw * v[4], vw * v[5],
                      0.0};
     store_partials(acc, 0, p.partials);

@@ -104,8 +104,11 @@ def test_add_potential_to_an_exported_bundle(ljx, tmp_path):
 
 
 @pytest.mark.gpu
-def test_reference_shaped_bundle_drives_the_engine(tmp_path):
+def test_reference_shaped_bundle_drives_the_engine(tmp_path, monkeypatch):
     import torch
+
+    # Every pair from both rows, no atomics (LJX_OWNED_HALF=0): two runs agree bit for bit.
+    monkeypatch.setenv("LJX_OWNED_HALF", "0")
 
     from cases import device_system, eam_case, write_eam_bundle
     ljx = load_package()

@@ -145,11 +145,13 @@ def test_spilled_groups_walk_their_lists(tmp_path, oracle):
                       "float64", case)
 
 
-def test_cache_build_is_deterministic(tmp_path):
+def test_cache_build_is_deterministic(tmp_path, monkeypatch):
     """The cache build numbers each union in first-seen order of one warp's walk over the
     group's lists, so a repeated run gives bitwise the same forces and energy on the build step
-    and on the cached steps after it. (Full list, newton off: every sum has a fixed order; the
+    and on the cached steps after it. (Full list, newton off, every pair evaluated from both of
+    its rows (LJX_OWNED_HALF=0): every sum has a fixed order. Holding owned pairs once and the
     newton-on modes scatter to neighbors with atomics.)"""
+    monkeypatch.setenv("LJX_OWNED_HALF", "0")
     mode = "rows-full"
     case = eam_case(elements=("Cu", "Zr"), cells=(5, 5, 5), seed=53, nr=2000, nrho=2000)
     rng = np.random.default_rng(8)
