@@ -267,9 +267,12 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
             if (r2 < p.model_cutsq) {
               const T r = pair_distance(r2);
               const int sj = static_cast<int>(xj.w);
-              rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+              // f_sj(r) to row i; f_si(r) to the neighbor (the same value for one species).
+              const T fj = spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+              rho += fj;
               if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
-                atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+                atomicAdd(p.rho + j,
+                          si == sj ? fj : spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
             }
           }
           if (MODE == kDensityHalfOwned)
@@ -306,9 +309,12 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
             }
             if (r2 < p.model_cutsq) {
               const T r = pair_distance(r2);
-              rho += spline_v<T>(p.density + static_cast<int>(xj.w) * p.nr, p.nr, r, p.inv_dr);
+              const int sj = static_cast<int>(xj.w);
+              const T fj = spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+              rho += fj;
               if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
-                atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+                atomicAdd(p.rho + j,
+                          si == sj ? fj : spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
             }
           }
           if (MODE == kDensityHalfOwned)

@@ -511,9 +511,12 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           if (slot < p.row_cap) crow[slot] = j;
           if (r2 < p.model_cutsq) {
             const T r = pair_distance(r2);
-            rho += spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+            // f_sj(r) to row i; f_si(r) to the neighbor, the same value for a same-species pair.
+            const T fj = spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+            rho += fj;
             if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
-              atomicAdd(p.rho + j, spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+              atomicAdd(p.rho + j,
+                        si == sj ? fj : spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
           }
         }
       };
