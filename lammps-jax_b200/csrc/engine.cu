@@ -470,6 +470,10 @@ void launch_density(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
   e->step_blocks[kDensityPart] = grid;
 }
 
+#ifndef LJX_BUILD_HALF_HASH
+#define LJX_BUILD_HALF_HASH 512
+#endif
+
 // Cache margin as a fraction of the pack cutoff: unions hold pairs within rc (1 + margin) and
 // stay valid until some atom has moved rc * margin / 2.
 constexpr double kGroupMargin = 0.08;
@@ -491,11 +495,16 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   const double cand = rc * (1.0 + kGroupMargin);
   const int span = std::min(p.nall, e->c.max_atoms);
   const int groups = (p.inum + ljx::kGroupRows - 1) / ljx::kGroupRows;
-  const int bgrid = std::max(1, std::min((groups + ljx::kBuildWarps - 1) / ljx::kBuildWarps,
-                                         e->sm_count * blocks_per_sm(ljx::k_build_groups<T>,
-                                                                     ljx::kBuildBlock)));
-  ljx::k_build_groups<T><<<bgrid, ljx::kBuildBlock, 0, s>>>(p, span, rebuild ? 1 : 0, disp_limit,
-                                                            cand * cand);
+  // Half rows (half lists, owned pairs held once) build with a set half the size.
+  auto build = [&](auto kernel) {
+    const int bgrid = std::max(1, std::min((groups + ljx::kBuildWarps - 1) / ljx::kBuildWarps,
+                                           e->sm_count * blocks_per_sm(kernel, ljx::kBuildBlock)));
+    kernel<<<bgrid, ljx::kBuildBlock, 0, s>>>(p, span, rebuild ? 1 : 0, disp_limit, cand * cand);
+  };
+  if (mode == ljx::kDensityHalf || mode == ljx::kDensityHalfOwned)
+    build(ljx::k_build_groups<T, LJX_BUILD_HALF_HASH>);
+  else
+    build(ljx::k_build_groups<T>);
   check_launch("k_build_groups");
   e->launches++;
   if (rebuild) e->group_builds++;

@@ -59,12 +59,17 @@ static_assert(kUnionMax < kHashSlots, "the set must keep free slots");
 // absent; a new atom takes the next union index, in first-seen order, and is written out at
 // once. Every candidate then goes straight into its row's slot list as its union index, so a
 // row's candidates keep the order of its LAMMPS list.
-template <typename T>
+// HASH: the set's slots. Rows that hold owned pairs once list about half the candidates, so
+// their builds use a set half the size (more resident warps); a group whose union passes three
+// quarters of the set is marked past capacity.
+template <typename T, int HASH = kHashSlots>
 __global__ void __launch_bounds__(kBuildBlock)
 k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, double cand_cutsq)
 {
-  __shared__ __align__(16) int s_key[kBuildWarps][kHashSlots];
-  __shared__ unsigned short s_index[kBuildWarps][kHashSlots];
+  static_assert((HASH & (HASH - 1)) == 0 && HASH >= 256 && HASH <= 1024, "power-of-two set");
+  constexpr int kHashShift = HASH == 1024 ? 22 : HASH == 512 ? 23 : 24;
+  __shared__ __align__(16) int s_key[kBuildWarps][HASH];
+  __shared__ unsigned short s_index[kBuildWarps][HASH];
   if (!force_build && !(__uint_as_float(*p.disp_bound) > disp_limit)) return;
   for (int a = blockIdx.x * blockDim.x + threadIdx.x; a < span; a += gridDim.x * blockDim.x)
     p.xref[a] = p.xd4[a];
@@ -77,7 +82,7 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
   const FilterBand band = filter_band(cand_cutsq, *p.coord_bound);
   const int groups = (p.inum + kGroupRows - 1) / kGroupRows;
   // The set starts empty; each group empties it again when done.
-  for (int h = lane; h < kHashSlots / 4; h += kWarp) key4[h] = make_int4(-1, -1, -1, -1);
+  for (int h = lane; h < HASH / 4; h += kWarp) key4[h] = make_int4(-1, -1, -1, -1);
   __syncwarp();
   for (int g = blockIdx.x * kBuildWarps + warp; g < groups; g += gridDim.x * kBuildWarps) {
     const int k = lane & (kGroupRows - 1);
@@ -116,11 +121,11 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
         }
       }
       // Multiplicative hash, linear probing.
-      unsigned h = (static_cast<unsigned>(j) * 0x9E3779B1u) >> 22;
+      unsigned h = (static_cast<unsigned>(j) * 0x9E3779B1u) >> kHashShift;
       bool fresh = false;
       if (cand) {
         bool placed = false;
-        for (int probe = 0; probe < kHashSlots; ++probe) {
+        for (int probe = 0; probe < HASH; ++probe) {
           int cur = key[h];
           if (cur == -1) cur = atomicCAS(const_cast<int *>(key) + h, -1, j);
           if (cur == -1 || cur == j) {
@@ -128,7 +133,7 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
             placed = true;
             break;
           }
-          h = (h + 1u) & (kHashSlots - 1);
+          h = (h + 1u) & (HASH - 1);
         }
         lost |= !placed;
       }
@@ -150,10 +155,10 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
     // A group that does not fit is marked past capacity; the density pass then walks its rows'
     // lists instead.
     const bool spilled = __any_sync(kFull, lost || got > p.rcap) || total > kUnionMax ||
-                         total > p.gcap;
+                         total > p.gcap || total > HASH * 3 / 4;
     if (lane < kGroupRows && row < p.inum) p.rcount[row] = got;
     __syncwarp();
-    for (int h = lane; h < kHashSlots / 4; h += kWarp) key4[h] = make_int4(-1, -1, -1, -1);
+    for (int h = lane; h < HASH / 4; h += kWarp) key4[h] = make_int4(-1, -1, -1, -1);
     __syncwarp();
     if (lane == 0) p.gcount[g] = spilled ? p.gcap + 1 : total;
   }
