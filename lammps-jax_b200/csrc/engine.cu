@@ -470,10 +470,6 @@ void launch_density(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
   e->step_blocks[kDensityPart] = grid;
 }
 
-#ifndef LJX_BUILD_HALF_HASH
-#define LJX_BUILD_HALF_HASH 512
-#endif
-
 // Cache margin as a fraction of the pack cutoff: unions hold pairs within rc (1 + margin) and
 // stay valid until some atom has moved rc * margin / 2.
 constexpr double kGroupMargin = 0.08;
@@ -521,8 +517,8 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
   };
   int grid = 0;
   if (mode == ljx::kDensityHalf)
-    grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityHalf, true>)
-                 : run(ljx::k_density_groups<T, ljx::kDensityHalf, false>);
+    grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityHalf, true, ljx::kHalfUnion>)
+                 : run(ljx::k_density_groups<T, ljx::kDensityHalf, false, ljx::kHalfUnion>);
   else if (mode == ljx::kDensityHalfOwned)
     grid = run(ljx::k_density_groups<T, ljx::kDensityHalfOwned, false>);
   else

@@ -35,6 +35,13 @@ constexpr int kUnionMax = 512;         // largest union a group may cache (share
 static_assert(kGroupRows == kWarpsPerBlock, "one warp per row of a group");
 static_assert(kGroupRows <= 8, "row masks are one byte");
 static_assert(kUnionMax < kHashSlots, "the set must keep free slots");
+// Builds over half rows (half lists, owned pairs held once) use a set of this many slots and
+// keep unions of at most three quarters of it; their density passes stage that many atoms.
+#ifndef LJX_BUILD_HALF_HASH
+#define LJX_BUILD_HALF_HASH 512
+#endif
+constexpr int kHalfUnion = LJX_BUILD_HALF_HASH * 3 / 4 < kUnionMax ? LJX_BUILD_HALF_HASH * 3 / 4
+                                                                   : kUnionMax;
 
 #ifndef LJX_GROUP_MIN_BLOCKS
 #define LJX_GROUP_MIN_BLOCKS 6
@@ -177,14 +184,19 @@ __device__ __forceinline__ double4 staged(const double2 *xy, const double2 *zw, 
 // well for half lists. Groups past capacity walk their rows' lists.
 // RULES: the bundle's packing has a half or unique-boundary rule to apply (half-edge bundles on
 // a full list); without one the keep test is the distance alone.
-template <typename T, int MODE, bool RULES = true>
+// UNION: the staged union's capacity. Builds over half rows mark unions past three quarters of
+// their 512-slot set as past capacity, so their cached groups stage at most 384 atoms; half
+// lists stage that much (less shared memory per block, more L1 left to the spline rows of two
+// species: C4 density -2 %), rows with owned pairs held once the full kUnionMax (C3: no gain).
+template <typename T, int MODE, bool RULES = true, int UNION = kUnionMax>
 __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
 {
+  static_assert(UNION <= kUnionMax, "the union stage holds at most kUnionMax atoms");
   // Staged positions as two 16-byte halves: consecutive slots then fall on different bank
   // quads (a 32-byte record per slot would reach only 4 of the 8 and conflict at least 2-way).
-  __shared__ double2 s_xy[kUnionMax];
-  __shared__ double2 s_zw[kUnionMax];
-  __shared__ int s_j[kUnionMax];
+  __shared__ double2 s_xy[UNION];
+  __shared__ double2 s_zw[UNION];
+  __shared__ int s_j[UNION];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
   const int groups = (p.inum + kGroupRows - 1) / kGroupRows;
@@ -192,7 +204,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
   int widest = 0;
   for (int g = blockIdx.x; g < groups; g += gridDim.x) {
     const int count = p.gcount[g];
-    const bool cached = count <= p.gcap;
+    const bool cached = count <= p.gcap && count <= UNION;
     // The warp's row and its first 32 candidate slots do not depend on the staged union: they
     // are loaded before the staging barrier, so their latency overlaps the staging gathers.
     // (rslot holds rcap >= 32 entries per row; slots past the row's count are not used.)
