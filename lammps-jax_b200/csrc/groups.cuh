@@ -307,7 +307,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
           double4 xj = make_double4(0.0, 0.0, 0.0, 0.0);
           if (jj < n) {
             j = p.neighbors[rowbase + static_cast<long long>(jj) * p.slot_stride] & kNeighMask;
-            if (j < p.max_atoms) {
+            if (j < p.max_atoms && !(p.half_rule && j < i)) {
               xj = load4(p.xd4 + j);
               keep = pack_keep(p, i, xi, j, xj);
             }

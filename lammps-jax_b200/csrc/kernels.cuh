@@ -555,7 +555,9 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           j = jj < kTileSlots ? s_tile[jj][warp]
                               : (p.neighbors[rowbase + static_cast<long long>(jj) * p.slot_stride] &
                                  kNeighMask);
-          if (j < p.max_atoms) {
+          // The half rule needs only the indices: a dropped pair costs no position gather
+          // (rows that hold owned pairs once drop about half their list this way).
+          if (j < p.max_atoms && !(p.half_rule && j < i)) {
             // Float pre-filter; only pairs inside the rounding band, or rows that need the
             // unique-boundary coordinate rule, read the double coordinates.
             const float4 fj = __ldg(pos4f + j);
@@ -852,7 +854,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
       const long long rowbase = static_cast<long long>(i) * p.atom_stride;
       for (int jj = lane; jj < listed; jj += kWarp) {
         const int j = p.neighbors[rowbase + jj * p.slot_stride] & kNeighMask;
-        if (j >= p.max_atoms) continue;
+        if (j >= p.max_atoms || (p.half_rule && j < i)) continue;
         if (pack_keep(p, i, xi, j, load4(p.xd4 + j))) {
           const V pj = load_pos(p, j);
           eam_edge<T, MODE, FORCES, TALLY, EV>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
