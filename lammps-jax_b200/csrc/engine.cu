@@ -472,7 +472,10 @@ void launch_density(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
 
 // Cache margin as a fraction of the pack cutoff: unions hold pairs within rc (1 + margin) and
 // stay valid until some atom has moved rc * margin / 2.
-constexpr double kGroupMargin = 0.08;
+#ifndef LJX_GROUP_MARGIN
+#define LJX_GROUP_MARGIN 0.08
+#endif
+constexpr double kGroupMargin = LJX_GROUP_MARGIN;
 // Shortest list lifetime (steps) for which the candidate cache is built.
 constexpr int kCacheMinPeriod = 4;
 
@@ -520,7 +523,7 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
     grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityHalf, true, ljx::kHalfUnion>)
                  : run(ljx::k_density_groups<T, ljx::kDensityHalf, false, ljx::kHalfUnion>);
   else if (mode == ljx::kDensityHalfOwned)
-    grid = run(ljx::k_density_groups<T, ljx::kDensityHalfOwned, false>);
+    grid = run(ljx::k_density_groups<T, ljx::kDensityHalfOwned, false, LJX_OWNED_UNION>);
   else
     grid = rules ? run(ljx::k_density_groups<T, ljx::kDensityFull, true>)
                  : run(ljx::k_density_groups<T, ljx::kDensityFull, false>);

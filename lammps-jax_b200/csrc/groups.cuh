@@ -43,13 +43,26 @@ static_assert(kUnionMax < kHashSlots, "the set must keep free slots");
 constexpr int kHalfUnion = LJX_BUILD_HALF_HASH * 3 / 4 < kUnionMax ? LJX_BUILD_HALF_HASH * 3 / 4
                                                                    : kUnionMax;
 
+#ifndef LJX_OWNED_UNION
+#define LJX_OWNED_UNION ljx::kUnionMax
+#endif
+// Resident blocks per SM of the cached density pass (caps its registers per thread). Rows of
+// owned pairs held once run 5 (48 registers, no spills, their candidate slots loaded ahead:
+// C3 density phase 2.35 -> 2.02 ms); the other modes 6 (40 registers; half lists: 5 blocks
+// were 5 % slower at C4).
 #ifndef LJX_GROUP_MIN_BLOCKS
 #define LJX_GROUP_MIN_BLOCKS 6
 #endif
-#if LJX_GROUP_MIN_BLOCKS > 0
-#define LJX_GROUP_BOUNDS __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS)
-#else
-#define LJX_GROUP_BOUNDS __launch_bounds__(kBlock)
+#ifndef LJX_GROUP_OWNED_MIN_BLOCKS
+#define LJX_GROUP_OWNED_MIN_BLOCKS 5
+#endif
+// Candidate slots of a row's second and third batches loaded before the staging barrier, per
+// mode (owned pairs held once / the others).
+#ifndef LJX_DG_PRELOAD_OWNED
+#define LJX_DG_PRELOAD_OWNED 1
+#endif
+#ifndef LJX_DG_PRELOAD
+#define LJX_DG_PRELOAD 0
 #endif
 
 // Rebuild the group caches when the host asks (new list, first use, changed sizes or pointers)
@@ -188,10 +201,20 @@ __device__ __forceinline__ double4 staged(const double2 *xy, const double2 *zw, 
 // their 512-slot set as past capacity, so their cached groups stage at most 384 atoms; half
 // lists stage that much (less shared memory per block, more L1 left to the spline rows of two
 // species: C4 density -2 %), rows with owned pairs held once the full kUnionMax (C3: no gain).
+template <int MODE>
+constexpr int group_min_blocks()
+{
+  return MODE == kDensityHalfOwned ? LJX_GROUP_OWNED_MIN_BLOCKS : LJX_GROUP_MIN_BLOCKS;
+}
+
 template <typename T, int MODE, bool RULES = true, int UNION = kUnionMax>
-__global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
+__global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
+    k_density_groups(const Step<T> p)
 {
   static_assert(UNION <= kUnionMax, "the union stage holds at most kUnionMax atoms");
+  // A row of owned pairs held once has about 72 candidates: with its first three batches'
+  // slots loaded before the staging barrier, its whole candidate list is in flight at once.
+  constexpr bool kPreload = MODE == kDensityHalfOwned ? LJX_DG_PRELOAD_OWNED : LJX_DG_PRELOAD;
   // Staged positions as two 16-byte halves: consecutive slots then fall on different bank
   // quads (a 32-byte record per slot would reach only 4 of the 8 and conflict at least 2-way).
   __shared__ double2 s_xy[UNION];
@@ -210,7 +233,7 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
     // (rslot holds rcap >= 32 entries per row; slots past the row's count are not used.)
     const int row = g * kGroupRows + warp;
     int i = -1, listed = 0, n = 0;
-    unsigned short slot0 = 0;
+    unsigned short slot0 = 0, slot1 = 0, slot2 = 0;
     double4 xi = make_double4(0.0, 0.0, 0.0, 0.0);
     if (row < p.inum) {
       i = p.ilist[row];
@@ -221,7 +244,12 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
       xi = load4(p.xd4 + i);
       if (cached) {
         n = p.rcount[row];
-        slot0 = load_once(p.rslot + static_cast<long long>(row) * p.rcap + lane);
+        const unsigned short *first = p.rslot + static_cast<long long>(row) * p.rcap + lane;
+        slot0 = load_once(first);
+        if constexpr (kPreload) {
+          if (lane + kWarp < p.rcap) slot1 = load_once(first + kWarp);
+          if (lane + 2 * kWarp < p.rcap) slot2 = load_once(first + 2 * kWarp);
+        }
       }
     }
     if (cached) {
@@ -258,7 +286,13 @@ __global__ void LJX_GROUP_BOUNDS k_density_groups(const Step<T> p)
           if (base + lane < n) {
             // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
             // staged coordinates.
-            slot = base == 0 ? slot0 : load_once(slots + base + lane);
+            if constexpr (kPreload)
+              slot = base == 0           ? slot0
+                     : base == kWarp     ? slot1
+                     : base == 2 * kWarp ? slot2
+                                         : load_once(slots + base + lane);
+            else
+              slot = base == 0 ? slot0 : load_once(slots + base + lane);
             xj = staged(s_xy, s_zw, slot);
             r2d = pack_r2(xi, xj);
             if constexpr (RULES) {

@@ -39,6 +39,9 @@ constexpr int kQueue = 64;
 // The force pass: 4 blocks of 256 per SM (64 registers); the double half-list variant, which
 // spills at 64, runs 3 (80 registers) and is faster for it. Force-only passes (no energy or
 // virial sums) hold 14 fewer registers per thread.
+#ifndef LJX_FORCE_EV_PRELOAD
+#define LJX_FORCE_EV_PRELOAD 0
+#endif
 #ifndef LJX_FORCE_ONLY_MIN_BLOCKS
 #define LJX_FORCE_ONLY_MIN_BLOCKS 4
 #endif
@@ -776,6 +779,12 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
   // one row ahead, so a row's dependent loads (atom -> position and F') start without waiting
   // on the list. The double full-list modes would spill at 64 registers, and lose.
   constexpr bool kAhead = sizeof(T) == 4 || MODE == kHalf;
+  // Double force-only passes load a row's first two batches of compacted neighbor indices
+  // together with the row's atom and kept count (they depend on the row alone), so a batch's
+  // position gathers do not wait on an index load (C3 force-only 1.744 -> 1.680 ms). With the
+  // energy and virial sums the two index registers spill at 64 registers, and at 3 blocks per
+  // SM the pass is no faster than without them.
+  constexpr int kPreloadIdx = sizeof(T) != 8 || TALLY ? 0 : !EV ? 2 : LJX_FORCE_EV_PRELOAD;
   const int stride = gridDim.x * kWarpsPerBlock;
   int row = blockIdx.x * kWarpsPerBlock + warp;
   int next_i = 0, next_n = 0;
@@ -785,6 +794,12 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
   }
   for (; row < p.inum; row += stride) {
     int i, n;
+    int j0 = 0, j1 = 0;
+    if constexpr (kPreloadIdx > 0) {
+      const int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
+      if (lane < p.row_cap) j0 = load_once(crow + lane);
+      if (kPreloadIdx > 1 && lane + kWarp < p.row_cap) j1 = load_once(crow + lane + kWarp);
+    }
     if constexpr (kAhead) {
       i = next_i;
       n = next_n;
@@ -811,7 +826,9 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
       if constexpr (sizeof(T) == 8) {
         // (Pipelining as below spills at 64 registers in double runs and loses.)
         for (int k = lane; k < n; k += kWarp) {
-          const int j = load_once(crow + k);
+          const int j = kPreloadIdx > 0 && k < kWarp       ? j0
+                        : kPreloadIdx > 1 && k < 2 * kWarp ? j1
+                                                           : load_once(crow + k);
           const V pj = load_pos(p, j);
           eam_edge<T, MODE, FORCES, TALLY, EV>(p, pi, si, fpi, j, pj, static_cast<int>(pj.w),
                                            kNeedFpj ? __ldg(p.fp + j) : T(0), fx, fy, fz, e, v,
