@@ -26,16 +26,22 @@ extern "C" {
 /* Device binning for ljx_neigh_build (no counterpart in the reference: LAMMPS bins inside
  * NPairKokkos): counting sort of the nall atoms of x into the grid given by lo, binsize and nbins
  * (HOST arrays), atoms in index order within each bin. bin_start receives nbins_total + 1 ints,
- * bin_atoms nall ints; scratch must hold nbins_total + ceil(nbins_total / 1024) ints. All three
- * are device memory owned by the caller; nothing is allocated. */
+ * bin_atoms nall ints; scratch must hold nbins_total + ceil(nbins_total / 1024) ints. sorted
+ * (16-byte aligned) receives nall + 1 records of 16 bytes: the atoms in bin order as float x, y,
+ * z and the atom index, then the largest |coordinate| that ljx_neigh_build's float distance test
+ * needs. All four are device memory owned by the caller; nothing is allocated. */
 ljx_status ljx_neigh_bin(void *stream, const double *x, int nall, const double *lo,
                          double binsize, const int *nbins, int *bin_start, int *bin_atoms,
-                         int *scratch);
+                         int *scratch, void *sorted);
 
+/* The list itself, from ljx_neigh_bin's bin_start, bin_atoms and sorted for the same x. Pairs are
+ * tested in float with a rounding band around the cutoff; those inside it take LAMMPS's double
+ * test, so the list is the double test's exactly. */
 ljx_status ljx_neigh_build(void *stream, const double *x, int nall, int nlocal, double cutoff,
                            int half, const double *lo, double binsize, const int *nbins,
-                           const int *bin_start, const int *bin_atoms, int *neighbors,
-                           long long slot_stride, int maxneigh, int *numneigh, int *widest);
+                           const int *bin_start, const int *bin_atoms, const void *sorted,
+                           int *neighbors, long long slot_stride, int maxneigh, int *numneigh,
+                           int *widest);
 
 #ifdef __cplusplus
 }

@@ -150,10 +150,10 @@ SIGNATURES = [
     ("ljx_pair_engine", c_void_p, [c_void_p]),
     ("ljx_version", c_char_p, []),
     ("ljx_neigh_bin", c_int, [c_void_p, c_void_p, c_int, c_void_p, c_double, c_void_p,
-                              c_void_p, c_void_p, c_void_p]),
+                              c_void_p, c_void_p, c_void_p, c_void_p]),
     ("ljx_neigh_build", c_int, [c_void_p, c_void_p, c_int, c_int, c_double, c_int, c_void_p,
-                                c_double, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong,
-                                c_int, c_void_p, c_void_p]),
+                                c_double, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_longlong, c_int, c_void_p, c_void_p]),
     ("ljx_nve_initial", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                 c_double, POINTER(c_double), c_int]),
     ("ljx_nve_final", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, POINTER(c_double),

@@ -1,14 +1,19 @@
 // Device neighbor-list build for the harness: bins of side >= cutoff / 2 (counting sort on the
-// device, ljx_neigh_bin), then one warp per bin scans the +-2 stencil (ljx_neigh_build) and
-// writes the bin's rows in Kokkos LayoutLeft.
+// device, ljx_neigh_bin, which also leaves a bin-ordered float copy of the positions), then one
+// warp per bin scans the +-2 stencil (ljx_neigh_build) and writes the bin's rows in Kokkos
+// LayoutLeft.
 
 #include <cuda_runtime.h>
 
 #include <algorithm>
 
+#include "kernels.cuh"
 #include "ljx_neigh.h"
 
 namespace {
+
+using ljx::FilterBand;
+using ljx::filter_band;
 
 struct Grid {
   double lo[3];
@@ -32,10 +37,19 @@ __device__ __forceinline__ long long bin_of(const double *x, int i, const Grid &
 // come out the same on every run.
 constexpr int kScanBlock = 1024;
 
-__global__ void k_bin_count(const double *__restrict__ x, int nall, Grid g, int *count)
+// Also the largest |coordinate| (float bits, of the float-rounded values) into *bound, which the
+// build's float distance test needs for its rounding band.
+__global__ void k_bin_count(const double *__restrict__ x, int nall, Grid g, int *count,
+                            unsigned int *bound)
 {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nall; i += gridDim.x * blockDim.x)
+  float big = 0.0f;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nall; i += gridDim.x * blockDim.x) {
     atomicAdd(count + bin_of(x, i, g), 1);
+    for (int k = 0; k < 3; ++k) big = fmaxf(big, fabsf(static_cast<float>(x[3 * i + k])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) big = fmaxf(big, __shfl_xor_sync(0xffffffffu, big, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(bound, __float_as_uint(big));
 }
 
 __global__ void k_scan_blocks(const int *__restrict__ count, long long nb, int *start,
@@ -101,13 +115,38 @@ __global__ void k_bin_order(const int *__restrict__ start, long long nb, int *bi
   }
 }
 
+// Bin-ordered float copy of the positions: record s holds atom bin_atoms[s] as (x, y, z, the
+// atom index's bits), so a stencil row's candidates are one contiguous run of records.
+__global__ void k_bin_sorted(const double *__restrict__ x, int nall,
+                             const int *__restrict__ bin_atoms, float4 *sorted)
+{
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < nall; s += gridDim.x * blockDim.x) {
+    const int j = bin_atoms[s];
+    sorted[s] = make_float4(static_cast<float>(x[3 * j]), static_cast<float>(x[3 * j + 1]),
+                            static_cast<float>(x[3 * j + 2]), __int_as_float(j));
+  }
+}
+
+// LAMMPS's distance test rsq < cutsq in double (npair: delx = xtmp - x[j][0], rsq = delx*delx +
+// dely*dely + delz*delz), without fused multiply-adds, for pairs the float test cannot decide.
+__device__ __forceinline__ bool within_exact(const double *xi, const double *__restrict__ x, int j,
+                                             double cutsq)
+{
+  const double ex = __dsub_rn(xi[0], x[3 * j]);
+  const double ey = __dsub_rn(xi[1], x[3 * j + 1]);
+  const double ez = __dsub_rn(xi[2], x[3 * j + 2]);
+  return __dadd_rn(__dadd_rn(__dmul_rn(ex, ex), __dmul_rn(ey, ey)), __dmul_rn(ez, ez)) < cutsq;
+}
+
 // One warp per bin: the bin's owned atoms (in index order, up to kRowsPerPass at a time) are
 // the rows; the atoms of the +-2 stencil are the candidates. For each (dy, dz) the five bins
-// along x are consecutive, so their atoms form one range of bin_atoms that the lanes read 32 at
-// a time; each candidate is tested against every row (row positions are shared-memory
-// broadcasts). Kept neighbors append to the rows in shared memory in stencil order; slots past
-// kRowCap go straight to global memory. The rows then leave slot-major, so one store covers the
-// same slot of consecutive rows (LayoutLeft).
+// along x are consecutive, so their atoms form one run of the bin-ordered float copy, which the
+// lanes read 32 records at a time (coalesced 16-byte loads). Each candidate is tested against
+// every row (row positions are shared-memory broadcasts) in float; only a pair whose float r^2
+// falls in the rounding band around the cutoff takes the exact double test. Kept neighbors
+// append to the rows in shared memory in stencil order; slots past kRowCap go straight to
+// global memory. The rows then leave slot-major, so one store covers the same slot of
+// consecutive rows (LayoutLeft).
 // Row staging capacity: 192 slots (24 KB per 4-warp block) measured faster than 256 (32 KB) at
 // 214 and 261 neighbors per row (C3, C5), by more resident blocks; the slots past it go
 // straight to global memory. 128 was slower again.
@@ -122,13 +161,14 @@ constexpr int kRowCap = LJX_NEIGH_ROW_CAP;
 constexpr int kNeighWarps = LJX_NEIGH_WARPS;
 
 __global__ void __launch_bounds__(kNeighWarps * 32)
-k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, Grid g,
+k_neigh_bins(const double *__restrict__ x, int nall, int nlocal, double cutsq, int half, Grid g,
              const int *__restrict__ bin_start, const int *__restrict__ bin_atoms,
-             int *__restrict__ neighbors, long long stride, int maxneigh,
-             int *__restrict__ numneigh, int *__restrict__ widest)
+             const float4 *__restrict__ sorted, int *__restrict__ neighbors, long long stride,
+             int maxneigh, int *__restrict__ numneigh, int *__restrict__ widest)
 {
   __shared__ int s_row[kNeighWarps][kRowsPerPass][kRowCap];
   __shared__ double s_xi[kNeighWarps][kRowsPerPass][3];
+  __shared__ float4 s_xf[kNeighWarps][kRowsPerPass];
   __shared__ int s_i[kNeighWarps][kRowsPerPass];
   __shared__ int s_start[kNeighWarps][32];  // stencil row q: first entry in bin_atoms
   __shared__ int s_off[kNeighWarps][32];    // stencil row q: offset in the candidate stream
@@ -137,8 +177,11 @@ k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, G
   const long long nbins = static_cast<long long>(g.nb[0]) * g.nb[1] * g.nb[2];
   int (*rows)[kRowCap] = s_row[warp];
   double (*xis)[3] = s_xi[warp];
+  float4 *xfs = s_xf[warp];
   int *is = s_i[warp];
   int wide = 0;
+  // The largest |coordinate| sits in the record after the last atom.
+  const FilterBand band = filter_band(cutsq, __float_as_uint(sorted[nall].x));
   for (long long b = static_cast<long long>(blockIdx.x) * kNeighWarps + warp; b < nbins;
        b += static_cast<long long>(gridDim.x) * kNeighWarps) {
     const int b0 = bin_start[b], b1 = bin_start[b + 1];
@@ -155,8 +198,10 @@ k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, G
     for (int r0 = 0; r0 < owned; r0 += kRowsPerPass) {
       const int m = min(kRowsPerPass, owned - r0);
       if (lane < m) {
-        const int i = bin_atoms[b0 + r0 + lane];
+        const float4 rf = sorted[b0 + r0 + lane];
+        const int i = __float_as_int(rf.w);
         is[lane] = i;
+        xfs[lane] = rf;
         xis[lane][0] = x[3 * i];
         xis[lane][1] = x[3 * i + 1];
         xis[lane][2] = x[3 * i + 2];
@@ -196,34 +241,34 @@ k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, G
       // batch, about one row, so the row only moves forward; the next batch's atom and position
       // are fetched before this batch's tests, so their latency overlaps them.
       int q = 0;
-      auto fetch = [&](int k, int &j, double &xa, double &ya, double &za) {
-        j = -1;
+      auto fetch = [&](int k, float4 &c) {
+        c.w = __int_as_float(-1);
         if (k < total) {
           while (q < 24 && s_off[warp][q + 1] <= k) ++q;
-          j = bin_atoms[s_start[warp][q] + (k - s_off[warp][q])];
-          xa = x[3 * j];
-          ya = x[3 * j + 1];
-          za = x[3 * j + 2];
+          c = sorted[s_start[warp][q] + (k - s_off[warp][q])];
         }
       };
-      int jn = -1;
-      double xn = 0, yn = 0, zn = 0;
-      fetch(lane, jn, xn, yn, zn);
+      float4 cn;
+      fetch(lane, cn);
       for (int s0 = 0; s0 < total; s0 += 32) {
-        const int j = jn;
-        const double xj = xn, yj = yn, zj = zn;
-        fetch(s0 + 32 + lane, jn, xn, yn, zn);
+        const float4 c = cn;
+        const int j = __float_as_int(c.w);
+        fetch(s0 + 32 + lane, cn);
 #pragma unroll
         for (int r = 0; r < kRowsPerPass; ++r) {
           if (r >= m) continue;  // m is the same for every lane
           const int i = is[r];
-          const double ex = xis[r][0] - xj, ey = xis[r][1] - yj, ez = xis[r][2] - zj;
-          bool keep = j >= 0 && j != i && ex * ex + ey * ey + ez * ez < cutsq;
+          const float4 rf = xfs[r];
+          const float dx = rf.x - c.x, dy = rf.y - c.y, dz = rf.z - c.z;
+          const float r2f = dx * dx + dy * dy + dz * dz;
+          bool keep = j >= 0 && j != i && r2f <= band.hi;
+          if (keep && r2f >= band.lo) keep = within_exact(xis[r], x, j, cutsq);
           if (keep && half) {
             if (j < nlocal) {
               keep = j > i;
             } else {
               const double zi = xis[r][2], yi = xis[r][1], xi = xis[r][0];
+              const double xj = x[3 * j], yj = x[3 * j + 1], zj = x[3 * j + 2];
               keep = !(zj < zi || (zj == zi && (yj < yi || (yj == yi && xj < xi))));
             }
           }
@@ -271,12 +316,13 @@ k_neigh_bins(const double *__restrict__ x, int nlocal, double cutsq, int half, G
 extern "C" ljx_status ljx_neigh_build(void *stream, const double *x, int nall, int nlocal,
                                       double cutoff, int half, const double *lo, double binsize,
                                       const int *nbins, const int *bin_start,
-                                      const int *bin_atoms, int *neighbors,
+                                      const int *bin_atoms, const void *sorted, int *neighbors,
                                       long long slot_stride, int maxneigh, int *numneigh,
                                       int *widest)
 {
   if (nlocal <= 0) return LJX_OK;
-  if (!x || !lo || !nbins || !bin_start || !bin_atoms || !neighbors || !numneigh || !widest ||
+  if (!x || !lo || !nbins || !bin_start || !bin_atoms || !sorted || !neighbors || !numneigh ||
+      !widest ||
       nall < nlocal || slot_stride < nlocal || maxneigh <= 0 || !(binsize >= 0.5 * cutoff) ||
       !(binsize > 0))
     return LJX_ERR_INVALID;
@@ -293,17 +339,19 @@ extern "C" ljx_status ljx_neigh_build(void *stream, const double *x, int nall, i
   const long long nb = static_cast<long long>(g.nb[0]) * g.nb[1] * g.nb[2];
   const long long blocks = std::min<long long>((nb + kNeighWarps - 1) / kNeighWarps, 148LL * 64);
   k_neigh_bins<<<static_cast<unsigned>(blocks), kNeighWarps * 32, 0, s>>>(
-      x, nlocal, cutoff * cutoff, half, g, bin_start, bin_atoms, neighbors, slot_stride, maxneigh,
-      numneigh, widest);
+      x, nall, nlocal, cutoff * cutoff, half, g, bin_start, bin_atoms,
+      static_cast<const float4 *>(sorted), neighbors, slot_stride, maxneigh, numneigh, widest);
   return cudaGetLastError() == cudaSuccess ? LJX_OK : LJX_ERR_CUDA;
 }
 
 extern "C" ljx_status ljx_neigh_bin(void *stream, const double *x, int nall, const double *lo,
                                     double binsize, const int *nbins, int *bin_start,
-                                    int *bin_atoms, int *scratch)
+                                    int *bin_atoms, int *scratch, void *sorted)
 {
-  if (!x || !lo || !nbins || !bin_start || !bin_atoms || !scratch || nall < 0 || !(binsize > 0))
+  if (!x || !lo || !nbins || !bin_start || !bin_atoms || !scratch || !sorted || nall < 0 ||
+      !(binsize > 0))
     return LJX_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(sorted) % alignof(float4) != 0) return LJX_ERR_INVALID;
   Grid g;
   long long nb = 1;
   for (int k = 0; k < 3; ++k) {
@@ -318,9 +366,14 @@ extern "C" ljx_status ljx_neigh_bin(void *stream, const double *x, int nall, con
   int *count = scratch;                // nb ints, then the per-bin cursors
   int *block_sums = scratch + nb;      // nblocks ints
   auto s = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(count, 0, nb * sizeof(int), s) != cudaSuccess) return LJX_ERR_CUDA;
+  float4 *records = static_cast<float4 *>(sorted);
+  // The record after the last atom carries the largest |coordinate| (float bits in .x).
+  unsigned int *bound = reinterpret_cast<unsigned int *>(records + nall);
+  if (cudaMemsetAsync(count, 0, nb * sizeof(int), s) != cudaSuccess ||
+      cudaMemsetAsync(records + nall, 0, sizeof(float4), s) != cudaSuccess)
+    return LJX_ERR_CUDA;
   const int flat = static_cast<int>(nall > 0 ? (nall + 255) / 256 : 1);
-  if (nall > 0) k_bin_count<<<flat, 256, 0, s>>>(x, nall, g, count);
+  if (nall > 0) k_bin_count<<<flat, 256, 0, s>>>(x, nall, g, count, bound);
   k_scan_blocks<<<static_cast<unsigned>(nblocks), kScanBlock, 0, s>>>(count, nb, bin_start,
                                                                        block_sums);
   k_scan_sums<<<1, 32, 0, s>>>(block_sums, static_cast<int>(nblocks), bin_start + nb);
@@ -328,5 +381,6 @@ extern "C" ljx_status ljx_neigh_bin(void *stream, const double *x, int nall, con
                                                                      count);
   if (nall > 0) k_bin_fill<<<flat, 256, 0, s>>>(x, nall, g, count, bin_atoms);
   k_bin_order<<<static_cast<unsigned>((nb + 255) / 256), 256, 0, s>>>(bin_start, nb, bin_atoms);
+  if (nall > 0) k_bin_sorted<<<flat, 256, 0, s>>>(x, nall, bin_atoms, records);
   return cudaGetLastError() == cudaSuccess ? LJX_OK : LJX_ERR_CUDA;
 }
