@@ -43,8 +43,11 @@ static_assert(kUnionMax < kHashSlots, "the set must keep free slots");
 constexpr int kHalfUnion = LJX_BUILD_HALF_HASH * 3 / 4 < kUnionMax ? LJX_BUILD_HALF_HASH * 3 / 4
                                                                    : kUnionMax;
 
+// Rows of owned pairs held once stage their unions twice over (one stage per group in turn, so
+// one block barrier per group instead of two), at most 384 atoms each: their builds already
+// mark larger unions past capacity. C3 density phase 2.020 -> 1.998 ms.
 #ifndef LJX_OWNED_UNION
-#define LJX_OWNED_UNION ljx::kUnionMax
+#define LJX_OWNED_UNION ljx::kHalfUnion
 #endif
 // Resident blocks per SM of the cached density pass (caps its registers per thread). Rows of
 // owned pairs held once run 5 (48 registers, no spills, their candidate slots loaded ahead:
@@ -63,6 +66,9 @@ constexpr int kHalfUnion = LJX_BUILD_HALF_HASH * 3 / 4 < kUnionMax ? LJX_BUILD_H
 #endif
 #ifndef LJX_DG_PRELOAD
 #define LJX_DG_PRELOAD 0
+#endif
+#ifndef LJX_DG_DOUBLE
+#define LJX_DG_DOUBLE 1
 #endif
 
 // Rebuild the group caches when the host asks (new list, first use, changed sizes or pointers)
@@ -200,7 +206,7 @@ __device__ __forceinline__ double4 staged(const double2 *xy, const double2 *zw, 
 // UNION: the staged union's capacity. Builds over half rows mark unions past three quarters of
 // their 512-slot set as past capacity, so their cached groups stage at most 384 atoms; half
 // lists stage that much (less shared memory per block, more L1 left to the spline rows of two
-// species: C4 density -2 %), rows with owned pairs held once the full kUnionMax (C3: no gain).
+// species: C4 density -2 %), and so do rows with owned pairs held once, in two stages.
 template <int MODE>
 constexpr int group_min_blocks()
 {
@@ -217,9 +223,14 @@ __global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
   constexpr bool kPreload = MODE == kDensityHalfOwned ? LJX_DG_PRELOAD_OWNED : LJX_DG_PRELOAD;
   // Staged positions as two 16-byte halves: consecutive slots then fall on different bank
   // quads (a 32-byte record per slot would reach only 4 of the 8 and conflict at least 2-way).
-  __shared__ double2 s_xy[UNION];
-  __shared__ double2 s_zw[UNION];
-  __shared__ int s_j[UNION];
+  // DOUBLE: two stages used in turn, so one barrier per group suffices (the stage written for
+  // group g + 2 was last read for group g, and every warp has passed group g + 1's barrier).
+  constexpr bool kDouble = MODE == kDensityHalfOwned && LJX_DG_DOUBLE;
+  constexpr int kStages = kDouble ? 2 : 1;
+  __shared__ double2 s_xy_all[kStages][UNION];
+  __shared__ double2 s_zw_all[kStages][UNION];
+  __shared__ int s_j_all[kStages][UNION];
+  int stage = 0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned below = (1u << lane) - 1u;
   const int groups = (p.inum + kGroupRows - 1) / kGroupRows;
@@ -228,6 +239,9 @@ __global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
   for (int g = blockIdx.x; g < groups; g += gridDim.x) {
     const int count = p.gcount[g];
     const bool cached = count <= p.gcap && count <= UNION;
+    double2 *s_xy = s_xy_all[stage], *s_zw = s_zw_all[stage];
+    int *s_j = s_j_all[stage];
+    if constexpr (kDouble) stage ^= 1;
     // The warp's row and its first 32 candidate slots do not depend on the staged union: they
     // are loaded before the staging barrier, so their latency overlaps the staging gathers.
     // (rslot holds rcap >= 32 entries per row; slots past the row's count are not used.)
@@ -319,11 +333,12 @@ __global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
               const T r = pair_distance(r2);
               const int sj = static_cast<int>(xj.w);
               // f_sj(r) to row i; f_si(r) to the neighbor (the same value for one species).
-              const T fj = spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+              const T fj = spline_v_dist<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
               rho += fj;
               if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
-                atomicAdd(p.rho + j,
-                          si == sj ? fj : spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+                atomicAdd(p.rho + j, si == sj ? fj
+                                              : spline_v_dist<T>(p.density + si * p.nr, p.nr, r,
+                                                                 p.inv_dr));
             }
           }
           if (MODE == kDensityHalfOwned)
@@ -361,11 +376,12 @@ __global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
             if (r2 < p.model_cutsq) {
               const T r = pair_distance(r2);
               const int sj = static_cast<int>(xj.w);
-              const T fj = spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+              const T fj = spline_v_dist<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
               rho += fj;
               if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
-                atomicAdd(p.rho + j,
-                          si == sj ? fj : spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+                atomicAdd(p.rho + j, si == sj ? fj
+                                              : spline_v_dist<T>(p.density + si * p.nr, p.nr, r,
+                                                                 p.inv_dr));
             }
           }
           if (MODE == kDensityHalfOwned)
@@ -383,7 +399,7 @@ __global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
       }
       kept_sum += kept + kept_twice;
     }
-    __syncthreads();
+    if constexpr (!kDouble) __syncthreads();
   }
   // kept_sum is carried by every lane of a warp: count it once.
   double acc[8] = {0, 0, 0, 0, 0, 0, 0, lane == 0 ? kept_sum : 0.0};

@@ -295,6 +295,19 @@ __device__ __forceinline__ T spline_v(const typename Vec4<T>::type *tab, int n, 
   return c.x + t * (c.y + t * (c.z + t * c.w));
 }
 
+// spline_v at a distance (x >= 0), where the node's lower clamp is a no-op and is left out, as
+// in the force pass (the same node, t and value; cached C3 density phase 1.999 -> 1.956 ms).
+template <typename T>
+__device__ __forceinline__ T spline_v_dist(const typename Vec4<T>::type *tab, int n, T x,
+                                           T inv_delta)
+{
+  const T idx = x * inv_delta;
+  const T fl = fmin(floor(idx), T(n - 2));
+  const T t = fmin(idx - fl, T(1));
+  const auto c = load4_tab(tab + static_cast<int>(fl));
+  return c.x + t * (c.y + t * (c.z + t * c.w));
+}
+
 template <typename T>
 __device__ __forceinline__ T spline_s(const typename Vec4<T>::type *tab, int n, T x, T inv_delta)
 {
@@ -515,11 +528,12 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           if (r2 < p.model_cutsq) {
             const T r = pair_distance(r2);
             // f_sj(r) to row i; f_si(r) to the neighbor, the same value for a same-species pair.
-            const T fj = spline_v<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
+            const T fj = spline_v_dist<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
             rho += fj;
             if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
-              atomicAdd(p.rho + j,
-                        si == sj ? fj : spline_v<T>(p.density + si * p.nr, p.nr, r, p.inv_dr));
+              atomicAdd(p.rho + j, si == sj ? fj
+                                            : spline_v_dist<T>(p.density + si * p.nr, p.nr, r,
+                                                               p.inv_dr));
           }
         }
       };
