@@ -43,21 +43,18 @@ static_assert(kUnionMax < kHashSlots, "the set must keep free slots");
 constexpr int kHalfUnion = LJX_BUILD_HALF_HASH * 3 / 4 < kUnionMax ? LJX_BUILD_HALF_HASH * 3 / 4
                                                                    : kUnionMax;
 
-// Rows of owned pairs held once stage their unions twice over (one stage per group in turn, so
-// one block barrier per group instead of two), at most 384 atoms each: their builds already
-// mark larger unions past capacity. C3 density phase 2.020 -> 1.998 ms.
+// Rows of owned pairs held once and half lists stage their unions twice over (one stage per
+// group in turn, so one block barrier per group instead of two), at most 384 atoms each: their
+// builds already mark larger unions past capacity. C3 density phase 2.020 -> 1.998 ms.
 #ifndef LJX_OWNED_UNION
 #define LJX_OWNED_UNION ljx::kHalfUnion
 #endif
-// Resident blocks per SM of the cached density pass (caps its registers per thread). Rows of
-// owned pairs held once run 5 (48 registers, no spills, their candidate slots loaded ahead:
-// C3 density phase 2.35 -> 2.02 ms); the other modes 6 (40 registers; half lists: 5 blocks
-// were 5 % slower at C4).
+// Resident blocks per SM of the cached density pass (caps its registers per thread): 5, at 48
+// registers without spills (6 blocks at 40 registers spilled: with owned pairs held once and
+// the candidate slots loaded ahead, C3 density phase 2.20 -> 2.02 ms; half lists with two union
+// stages, C4 at 80^3 1.605 -> 1.588 ms; full rows 2.975 -> 2.898 ms).
 #ifndef LJX_GROUP_MIN_BLOCKS
-#define LJX_GROUP_MIN_BLOCKS 6
-#endif
-#ifndef LJX_GROUP_OWNED_MIN_BLOCKS
-#define LJX_GROUP_OWNED_MIN_BLOCKS 5
+#define LJX_GROUP_MIN_BLOCKS 5
 #endif
 // Candidate slots of a row's second and third batches loaded before the staging barrier, per
 // mode (owned pairs held once / the others).
@@ -69,6 +66,9 @@ constexpr int kHalfUnion = LJX_BUILD_HALF_HASH * 3 / 4 < kUnionMax ? LJX_BUILD_H
 #endif
 #ifndef LJX_DG_DOUBLE
 #define LJX_DG_DOUBLE 1
+#endif
+#ifndef LJX_DG_DOUBLE_HALF
+#define LJX_DG_DOUBLE_HALF 1
 #endif
 
 // Rebuild the group caches when the host asks (new list, first use, changed sizes or pointers)
@@ -207,15 +207,8 @@ __device__ __forceinline__ double4 staged(const double2 *xy, const double2 *zw, 
 // their 512-slot set as past capacity, so their cached groups stage at most 384 atoms; half
 // lists stage that much (less shared memory per block, more L1 left to the spline rows of two
 // species: C4 density -2 %), and so do rows with owned pairs held once, in two stages.
-template <int MODE>
-constexpr int group_min_blocks()
-{
-  return MODE == kDensityHalfOwned ? LJX_GROUP_OWNED_MIN_BLOCKS : LJX_GROUP_MIN_BLOCKS;
-}
-
 template <typename T, int MODE, bool RULES = true, int UNION = kUnionMax>
-__global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
-    k_density_groups(const Step<T> p)
+__global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups(const Step<T> p)
 {
   static_assert(UNION <= kUnionMax, "the union stage holds at most kUnionMax atoms");
   // A row of owned pairs held once has about 72 candidates: with its first three batches'
@@ -225,7 +218,8 @@ __global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
   // quads (a 32-byte record per slot would reach only 4 of the 8 and conflict at least 2-way).
   // DOUBLE: two stages used in turn, so one barrier per group suffices (the stage written for
   // group g + 2 was last read for group g, and every warp has passed group g + 1's barrier).
-  constexpr bool kDouble = MODE == kDensityHalfOwned && LJX_DG_DOUBLE;
+  constexpr bool kDouble = (MODE == kDensityHalfOwned && LJX_DG_DOUBLE) ||
+                           (MODE == kDensityHalf && LJX_DG_DOUBLE_HALF);
   constexpr int kStages = kDouble ? 2 : 1;
   __shared__ double2 s_xy_all[kStages][UNION];
   __shared__ double2 s_zw_all[kStages][UNION];
@@ -290,55 +284,62 @@ __global__ void __launch_bounds__(kBlock, group_min_blocks<MODE>())
       if (cached) {
         // About 80 % of a row's cached candidates are kept, so each batch of 32 evaluates its
         // kept pairs in place: the idle lanes cost little (a gather costs per sector touched,
-        // not per lane) and no queue round trip through shared memory is needed.
+        // not per lane) and no queue round trip through shared memory is needed. The reference's
+        // keep test in double (pair_jax_kokkos.cpp:84-101) runs straight from the staged
+        // coordinates. The batch is predicated: every lane runs the keep test and the table-node
+        // arithmetic of spline_v_dist (lanes past the row's candidates on slot 0 of the stage),
+        // and only the table gather, the compacted store and the neighbor's reduction depend on
+        // the lane's pair. (Nested divergent branches had cost 83 branch instructions per row:
+        // C3 density phase 1.961 -> 1.843 ms, f32 1.769 -> 1.634 ms, C4 at 80^3 1.582 -> 1.560.)
         const unsigned short *slots = p.rslot + static_cast<long long>(row) * p.rcap;
         for (int base = 0; base < n; base += kWarp) {
-          int slot = 0, j = 0;
-          bool keep = false;
-          double r2d = 0.0;
-          double4 xj = make_double4(0.0, 0.0, 0.0, 0.0);
-          if (base + lane < n) {
-            // The reference's keep test in double (pair_jax_kokkos.cpp:84-101) straight from the
-            // staged coordinates.
-            if constexpr (kPreload)
-              slot = base == 0           ? slot0
-                     : base == kWarp     ? slot1
-                     : base == 2 * kWarp ? slot2
-                                         : load_once(slots + base + lane);
-            else
-              slot = base == 0 ? slot0 : load_once(slots + base + lane);
-            xj = staged(s_xy, s_zw, slot);
-            r2d = pack_r2(xi, xj);
-            if constexpr (RULES) {
-              j = s_j[slot];
-              keep = r2d <= p.pack_cutsq && pair_rules(p, i, xi, j, xj);
-            } else {
-              keep = r2d <= p.pack_cutsq;
-            }
-          }
+          const bool valid = base + lane < n;
+          int slot;
+          if constexpr (kPreload)
+            slot = base == 0           ? slot0
+                   : base == kWarp     ? slot1
+                   : base == 2 * kWarp ? slot2
+                   : valid             ? load_once(slots + base + lane)
+                                       : 0;
+          else
+            slot = base == 0 ? slot0 : valid ? load_once(slots + base + lane) : 0;
+          slot = valid ? slot : 0;
+          const double4 xj = staged(s_xy, s_zw, slot);
+          const double r2d = pack_r2(xi, xj);
+          const int j = s_j[slot];
+          bool keep = valid && r2d <= p.pack_cutsq;
+          if constexpr (RULES) keep = keep && pair_rules(p, i, xi, j, xj);
           const unsigned m = __ballot_sync(kFull, keep);
-          if (keep) {
-            if constexpr (!RULES) j = s_j[slot];
-            const int at = kept + __popc(m & below);
-            if (at < p.row_cap) crow[at] = j;
-            T r2;
-            if constexpr (sizeof(T) == 8) {
-              r2 = r2d;  // the model's double r^2 is the reference's pack r^2
-            } else {
-              const float dx = static_cast<float>(xj.x) - fix, dy = static_cast<float>(xj.y) - fiy,
-                          dz = static_cast<float>(xj.z) - fiz;
-              r2 = dx * dx + dy * dy + dz * dz;
-            }
-            if (r2 < p.model_cutsq) {
-              const T r = pair_distance(r2);
-              const int sj = static_cast<int>(xj.w);
-              // f_sj(r) to row i; f_si(r) to the neighbor (the same value for one species).
-              const T fj = spline_v_dist<T>(p.density + sj * p.nr, p.nr, r, p.inv_dr);
-              rho += fj;
-              if (MODE == kDensityHalf || (MODE == kDensityHalfOwned && j < p.nlocal))
-                atomicAdd(p.rho + j, si == sj ? fj
-                                              : spline_v_dist<T>(p.density + si * p.nr, p.nr, r,
-                                                                 p.inv_dr));
+          const int at = kept + __popc(m & below);
+          if (keep && at < p.row_cap) crow[at] = j;
+          T r2;
+          if constexpr (sizeof(T) == 8) {
+            r2 = r2d;
+          } else {
+            const float dx = static_cast<float>(xj.x) - fix, dy = static_cast<float>(xj.y) - fiy,
+                        dz = static_cast<float>(xj.z) - fiz;
+            r2 = dx * dx + dy * dy + dz * dz;
+          }
+          const bool ev = keep && r2 < p.model_cutsq;
+          const int sj = static_cast<int>(xj.w);
+          const T idx = pair_distance(r2) * p.inv_dr;
+          const T fl = fmin(floor(idx), T(p.nr - 2));
+          const T t = fmin(idx - fl, T(1));
+          const int node = static_cast<int>(fl);
+          T fj = T(0);
+          if (ev) {
+            const auto c = load4_tab(p.density + sj * p.nr + node);
+            fj = c.x + t * (c.y + t * (c.z + t * c.w));
+          }
+          rho += fj;
+          if (MODE == kDensityHalf || MODE == kDensityHalfOwned) {
+            if (ev && (MODE == kDensityHalf || j < p.nlocal)) {
+              T fi = fj;
+              if (si != sj) {
+                const auto c = load4_tab(p.density + si * p.nr + node);
+                fi = c.x + t * (c.y + t * (c.z + t * c.w));
+              }
+              atomicAdd(p.rho + j, fi);
             }
           }
           if (MODE == kDensityHalfOwned)
