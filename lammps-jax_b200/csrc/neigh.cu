@@ -160,8 +160,10 @@ constexpr int kRowsPerPass = 8;
 constexpr int kRowCap = LJX_NEIGH_ROW_CAP;
 constexpr int kNeighWarps = LJX_NEIGH_WARPS;
 
+// HALF: keep each pair once (owned j > i, a ghost j only if it sorts after i in (z, y, x)).
+template <bool HALF>
 __global__ void __launch_bounds__(kNeighWarps * 32)
-k_neigh_bins(const double *__restrict__ x, int nall, int nlocal, double cutsq, int half, Grid g,
+k_neigh_bins(const double *__restrict__ x, int nall, int nlocal, double cutsq, Grid g,
              const int *__restrict__ bin_start, const int *__restrict__ bin_atoms,
              const float4 *__restrict__ sorted, int *__restrict__ neighbors, long long stride,
              int maxneigh, int *__restrict__ numneigh, int *__restrict__ widest)
@@ -241,8 +243,9 @@ k_neigh_bins(const double *__restrict__ x, int nall, int nlocal, double cutsq, i
       // batch, about one row, so the row only moves forward; the next batch's atom and position
       // are fetched before this batch's tests, so their latency overlaps them.
       int q = 0;
+      // Past the stream's end a lane holds an atom at infinity (index -1), which no row keeps.
       auto fetch = [&](int k, float4 &c) {
-        c.w = __int_as_float(-1);
+        c = make_float4(INFINITY, INFINITY, INFINITY, __int_as_float(-1));
         if (k < total) {
           while (q < 24 && s_off[warp][q + 1] <= k) ++q;
           c = sorted[s_start[warp][q] + (k - s_off[warp][q])];
@@ -261,25 +264,29 @@ k_neigh_bins(const double *__restrict__ x, int nall, int nlocal, double cutsq, i
           const float4 rf = xfs[r];
           const float dx = rf.x - c.x, dy = rf.y - c.y, dz = rf.z - c.z;
           const float r2f = dx * dx + dy * dy + dz * dz;
-          bool keep = j >= 0 && j != i && r2f <= band.hi;
-          if (keep && r2f >= band.lo) keep = within_exact(xis[r], x, j, cutsq);
-          if (keep && half) {
-            if (j < nlocal) {
-              keep = j > i;
-            } else {
-              const double zi = xis[r][2], yi = xis[r][1], xi = xis[r][0];
-              const double xj = x[3 * j], yj = x[3 * j + 1], zj = x[3 * j + 2];
-              keep = !(zj < zi || (zj == zi && (yj < yi || (yj == yi && xj < xi))));
+          bool keep = j != i && r2f <= band.hi;
+          // Predicated: the rare pair inside the band takes the double test under a warp vote,
+          // so the common batch runs without divergent branches.
+          const bool unsure = keep && r2f >= band.lo;
+          if (__any_sync(0xffffffffu, unsure)) {
+            if (unsure) keep = within_exact(xis[r], x, j, cutsq);
+          }
+          if constexpr (HALF) {
+            if (keep) {
+              if (j < nlocal) {
+                keep = j > i;
+              } else {
+                const double zi = xis[r][2], yi = xis[r][1], xi = xis[r][0];
+                const double xj = x[3 * j], yj = x[3 * j + 1], zj = x[3 * j + 2];
+                keep = !(zj < zi || (zj == zi && (yj < yi || (yj == yi && xj < xi))));
+              }
             }
           }
           const unsigned mk = __ballot_sync(0xffffffffu, keep);
-          if (keep) {
-            const int slot = count[r] + __popc(mk & below);
-            if (slot < kRowCap)
-              rows[r][slot] = j;
-            else if (slot < maxneigh)
-              neighbors[i + static_cast<long long>(slot) * stride] = j;
-          }
+          const int slot = count[r] + __popc(mk & below);
+          if (keep && slot < kRowCap) rows[r][slot] = j;
+          if (keep && slot >= kRowCap && slot < maxneigh)
+            neighbors[i + static_cast<long long>(slot) * stride] = j;
           count[r] += __popc(mk);
         }
       }
@@ -338,8 +345,9 @@ extern "C" ljx_status ljx_neigh_build(void *stream, const double *x, int nall, i
   if (cudaMemsetAsync(widest, 0, sizeof(int), s) != cudaSuccess) return LJX_ERR_CUDA;
   const long long nb = static_cast<long long>(g.nb[0]) * g.nb[1] * g.nb[2];
   const long long blocks = std::min<long long>((nb + kNeighWarps - 1) / kNeighWarps, 148LL * 64);
-  k_neigh_bins<<<static_cast<unsigned>(blocks), kNeighWarps * 32, 0, s>>>(
-      x, nall, nlocal, cutoff * cutoff, half, g, bin_start, bin_atoms,
+  auto kernel = half ? k_neigh_bins<true> : k_neigh_bins<false>;
+  kernel<<<static_cast<unsigned>(blocks), kNeighWarps * 32, 0, s>>>(
+      x, nall, nlocal, cutoff * cutoff, g, bin_start, bin_atoms,
       static_cast<const float4 *>(sorted), neighbors, slot_stride, maxneigh, numneigh, widest);
   return cudaGetLastError() == cudaSuccess ? LJX_OK : LJX_ERR_CUDA;
 }
