@@ -401,9 +401,22 @@ def run_ljx(args):
                      real * nlocal)
     pos_bytes = 32 if precision == "float64" else 16
     bytes_force = 8 * nlocal + 4 * kept_local + pos_bytes * nall + real * nall + 48 * nlocal
-    kernel = max(("density", "force"), key=lambda n: phase[n])
+    # The line's roofline is the phase that moves most of the step's algorithmic bytes: the
+    # density phase, which carries the list read. (By time the density and force phases are
+    # about equal at C3, so a choice by time would flip between runs.) Both phases and the whole
+    # step are reported beside it.
+    kernel = "density" if bytes_density >= bytes_force else "force"
     kbytes = bytes_density if kernel == "density" else bytes_force
     achieved = kbytes / phase[kernel] / 1e9
+    # Whole step: every row's list slots and count read, each kept edge written once and its
+    # index read twice (density and force passes), and per owned atom x read by three passes
+    # (24 B each), type, rho written, F' written and read, f read-modify-written (double); per
+    # ghost x three times, type and F' (newton on adds the ghost's rho and f round trips).
+    newton = bool(system.newton_pair)
+    b_own = 3 * 24 + 4 + real + 2 * real + 48
+    b_ghost = 3 * 24 + 4 + real + ((2 * real + 48) if newton else 0)
+    bytes_step = (4 * listed + 4 * nlocal + 12 * kept_local + nlocal * b_own +
+                  (nall - nlocal) * b_ghost)
     peak, peak_kind = peaks()
     # The engine caches candidates only for lists that live at least 4 steps (kCacheMinPeriod in
     # csrc/engine.cu); shorter-lived lists take the list pass.
@@ -481,7 +494,21 @@ def run_ljx(args):
                                     "(list read every step); with the candidate cache the list "
                                     "is read only at rebuilds, so this is an effective bandwidth"
                                     if kernel == "density" and cached else
-                                    "per-launch algorithmic bytes"},
+                                    "per-launch algorithmic bytes",
+                     "why_this_kernel": "the phase with the larger algorithmic bytes per step "
+                                        "(the density phase carries the list read)",
+                     "phases": {
+                         n: {"ms": phase[n] * 1e3, "algorithmic_bytes": b,
+                             "achieved": b / phase[n] / 1e9,
+                             "frac": b / phase[n] / 1e9 / peak}
+                         for n, b in (("density", bytes_density), ("force", bytes_force))},
+                     "step": {"ms": elapsed / args.steps * 1e3,
+                              "algorithmic_bytes": bytes_step,
+                              "achieved": bytes_step / (elapsed / args.steps) / 1e9,
+                              "frac": bytes_step / (elapsed / args.steps) / 1e9 / peak,
+                              "basis": "whole step: list slots and counts read, kept edges "
+                                       "written once and read twice, per-atom x, type, rho, "
+                                       "F' and f traffic"}},
         "gpu_launches": launches,
         "e2e": e2e,
         "energy_per_atom": energy_total / total_atoms,
