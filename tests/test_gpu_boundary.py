@@ -22,9 +22,10 @@ import numpy as np
 import pytest
 import torch
 
-from cases import Case, canonical_edges, copy_device, device_system, host_list, write_eam_bundle
+from cases import (F32_FORCE_REL, F32_TOTAL_REL, F64_FORCE_REL, F64_TOTAL_REL, Case,
+                   canonical_edges, copy_device, device_system, host_list, write_eam_bundle)
 from conftest import load_package
-from test_gpu_parity import MODE_SETUP, assert_parity, oracle_step
+from test_gpu_parity import LJ_MODES, MODE_SETUP, assert_parity, oracle_step
 
 SPACING = 3.25
 CELLS = 7
@@ -144,3 +145,47 @@ def test_boundary_eam_step(tmp_path, oracle, mode, cache, precision):
     torch.cuda.synchronize()
     ref = oracle_step(oracle, case, system, mode, precision)
     assert_parity(res, system, ref, precision, case)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision", ["float64", "float32"])
+@pytest.mark.parametrize("mode", list(LJ_MODES))
+def test_boundary_lj_step(tmp_path, oracle, mode, precision):
+    """LJ does not vanish at the cutoff, so a pair on rc that the model evaluated (r^2 <= rc^2
+    instead of r^2 < rc^2) would show in the forces and the energy; the kept count checks the
+    pack's r^2 <= rc^2. sigma = 2.9 puts the spacing near the potential's minimum."""
+    ljx = load_package()
+    force_output, newton, half = LJ_MODES[mode]
+    case = boundary_case()
+    nall, nlocal = len(case.x_all), case.nlocal
+    sigma = 2.9
+    path = tmp_path / "lj.json"
+    ljx.write_bundle(path, potential=ljx.lj_potential(1.0, sigma), max_atoms=nall + 32,
+                     max_edges=(nall + 32) * 96, cutoff=case.cutoff, unit_style="lj",
+                     precision=precision, force_output=force_output,
+                     newton="on" if newton else "off")
+    x = torch.as_tensor(case.x_all, device="cuda")
+    system = ljx.System(x=x, type=torch.ones(nall, dtype=torch.int32, device="cuda"),
+                        f=torch.zeros_like(x), nlocal=nlocal, nghost=nall - nlocal,
+                        newton_pair=newton, unit_style="lj", ntypes=1)
+    system.list = ljx.synth.neighbor_list(case.x_all, nlocal, case.cutoff + case.skin, half=half)
+    system.comm = ljx.SelfComm(torch.as_tensor(case.owner, device="cuda"), nlocal)
+    pair = ljx.PairJax()
+    pair.coeff(system, "*", "*", str(path))
+    pair.init_style(system)
+    res = pair.compute(system)
+    if newton:
+        system.comm.reverse_forces(system.f)
+    torch.cuda.synchronize()
+    ref = oracle.lj_step(case.x_all, nlocal, case.owner, host_list(system.list), epsilon=1.0,
+                         sigma=sigma, cutoff=case.cutoff, force_output=force_output,
+                         newton_pair=newton, precision=precision)
+    forces = system.f[:nlocal].cpu().numpy()
+    fmax = float(np.max(np.abs(ref.forces)))
+    frel = F64_FORCE_REL if precision == "float64" else F32_FORCE_REL
+    trel = F64_TOTAL_REL if precision == "float64" else F32_TOTAL_REL
+    assert float(np.max(np.abs(forces - ref.forces))) <= frel * fmax
+    assert res.energy == pytest.approx(ref.energy, rel=trel)
+    vscale = float(np.max(np.abs(ref.virial)))
+    assert float(np.max(np.abs(np.array(res.virial) - ref.virial))) <= trel * vscale
+    assert res.edge_count == ref.count
