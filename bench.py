@@ -219,6 +219,7 @@ class Case:
         self.halo = self.decomp.get("halo")
         self.stream = torch.cuda.current_stream()
         self.tick = 0
+        self.fp_overlap = False
 
     def streams_rows(self):
         """Whether the force pass can stream its rows to the host (each list row holds its
@@ -243,10 +244,18 @@ class Case:
         mark(2)
         eng.embed(atoms)
         mark(3)
-        if self.plan.forward_fp:
+        # Across GPUs the F' exchange can run on a side stream under the force pass's rows that
+        # keep no ghost neighbor (NcclHalo.forward_under_force); the halo_fp phase is then only
+        # the launch, and the force phase holds any wait for the exchange.
+        overlap = (self.fp_overlap and self.halo is not None and self.plan.forward_fp and
+                   f_host is None and ev)
+        if self.plan.forward_fp and not overlap:
             s.comm.forward(self.fp_rows, self.width, self.elem)
         mark(4)
-        if f_host is not None:
+        if overlap:
+            self.halo.forward_under_force(eng, atoms, nl, newton, self.fp_rows, self.width,
+                                          self.elem)
+        elif f_host is not None:
             eng.force_to_host(atoms, nl, newton, f_host, 1.0, pieces)
         elif not ev:
             eng.force_only(atoms, nl, newton, 1.0)
@@ -382,6 +391,7 @@ def run_ljx(args):
     if cfg.get("one_gpu") and world > 1:
         raise SystemExit(f"--config {args.config} runs on one GPU")
     case = Case(ljx, args.config, precision, world, rank, local, args.cells)
+    case.fp_overlap = args.fp_overlap == "on"
     system, nlocal, nall, decomp = case.system, case.nlocal, case.nall, case.decomp
 
     # The clock samples span the warm-up and the timed steps (both under load); they go to a
@@ -565,6 +575,7 @@ def run_c4(ljx, args, world, rank, local):
     forces that let runs at different GPU counts be compared atom by atom."""
     import torch
     case = Case(ljx, "c4", "float64", world, rank, local)
+    case.fp_overlap = args.fp_overlap == "on"
     timing = case.time(args.steps, args.warmup, 10)
     total = case.total_atoms()
     sample_ids = np.linspace(0, total - 1, C4_SAMPLES).astype(np.int64)
@@ -948,6 +959,9 @@ def main():
     ap.add_argument("--e2e-pieces", type=int, default=8,
                     help="row pieces of the e2e force pass whose force rows are copied to the "
                          "host as each finishes (ljx_force_to_host); 0: one copy after the step")
+    ap.add_argument("--fp-overlap", choices=("on", "off"), default="on",
+                    help="across GPUs, run the F' exchange under the force pass's rows without "
+                         "ghost neighbors (ljx_force_rows)")
     ap.add_argument("--quick", action="store_true",
                     help="time the device path, the e2e and the force-only legs only (no MD, "
                          "C4, float32 or CPU-baseline legs)")

@@ -89,6 +89,9 @@ class Plan(Structure):
 
 
 # Every symbol the headers declare: (name, restype, argtypes).
+ROWS_LOCAL = 1  # ljx_force_rows parts (include/ljx.h)
+ROWS_GHOST = 2
+
 SIGNATURES = [
     ("ljx_bundle_load", c_int, [c_char_p, POINTER(c_void_p)]),
     ("ljx_bundle_load_string", c_int, [c_char_p, c_size_t, POINTER(c_void_p)]),
@@ -110,6 +113,8 @@ SIGNATURES = [
     ("ljx_embed", c_int, [c_void_p, c_void_p, POINTER(Atoms)]),
     ("ljx_force", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
                           c_double]),
+    ("ljx_force_rows", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
+                               c_double, c_int]),
     ("ljx_force_only", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,
                                c_double]),
     ("ljx_force_to_host", c_int, [c_void_p, c_void_p, POINTER(Atoms), POINTER(NeighList), c_int,

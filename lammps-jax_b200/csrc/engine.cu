@@ -101,6 +101,7 @@ struct ljx_engine {
   void *fp = nullptr;
   int *cedges = nullptr;
   int *ccount = nullptr;
+  unsigned char *ghost_rows = nullptr;  // per list row: keeps a ghost neighbor (density passes)
   void *embedding = nullptr;
   void *density = nullptr;
   void *density_slope = nullptr;
@@ -163,6 +164,9 @@ struct ljx_engine {
   bool step_ev = true;            // false after ljx_force_only: the result has no energy/virial
   bool owned_half = true;         // allow owned pairs held once (LJX_OWNED_HALF, default on)
   bool rows_owned_half = false;   // the last ljx_density compacted rows that hold them once
+  // ljx_force_rows: partial rows of this step's local-rows pass, which the ghost-rows pass
+  // writes after (-1: no local-rows pass since the last ljx_density).
+  int local_part_blocks = -1;
   std::string error;
 
   ~ljx_engine()
@@ -174,7 +178,8 @@ struct ljx_engine {
     void *ptrs[] = {xd4,       pos4,      rho,        fp,          cedges,  ccount,
                     embedding, density,   density_slope, pair,     coord_bound, xref,
                     gatom,     gcount,    rslot,      rcount,      senders,
-                    receivers, edge_mask, offsets,    count_prev,  partials, result};
+                    receivers, edge_mask, offsets,    count_prev,  partials, result,
+                    ghost_rows};
     for (void *p : ptrs)
       if (p) cudaFree(p);
     if (host_result) cudaFreeHost(host_result);
@@ -355,6 +360,8 @@ ljx::Step<T> make_step(ljx_engine *e, const ljx_atoms *a, const ljx_list *l, dou
   p.fp = static_cast<T *>(e->fp);
   p.cedges = e->cedges;
   p.ccount = e->ccount;
+  p.ghost_rows = e->ghost_rows;
+  p.row_part = ljx::kRowsAll;
   p.row_cap = e->row_cap;
   p.embedding = static_cast<const V *>(e->embedding);
   p.density = static_cast<const V *>(e->density);
@@ -647,6 +654,7 @@ ljx_status density_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const
                         int newton_pair)
 {
   const Modes m = density_modes(e, newton_pair, l ? l->inum : 0, a ? a->nlocal : 0);
+  e->local_part_blocks = -1;
   if (e->c.potential == LJX_POTENTIAL_LJ) return LJX_OK;  // LJ is one pass (ljx_force)
   ljx::Step<T> p = make_step<T>(e, a, l, 1.0);
   set_pack_rules(p, e->c, m);
@@ -717,6 +725,36 @@ ljx_status force_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const l
   }
   p.partials = e->partial(kForcePart);
   launch_force<T>(e, s, p, m.force);
+  return LJX_OK;
+}
+
+// One part of the EAM force pass (ljx_force_rows): the list rows that keep no ghost neighbor
+// (LJX_ROWS_LOCAL) or the others (LJX_ROWS_GHOST), as this step's ljx_density marked them. The
+// local rows read no ghost F', so they can run while the F' exchange is in flight. The ghost
+// part writes its energy and virial partial rows after the local part's, so the step's result
+// sums both.
+template <typename T>
+ljx_status force_rows_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
+                           int newton_pair, double scale, int part)
+{
+  if (e->c.potential != LJX_POTENTIAL_EAM)
+    return fail(e, LJX_ERR_UNSUPPORTED, "the force pass splits by ghost rows for EAM bundles only");
+  if (part != LJX_ROWS_LOCAL && part != LJX_ROWS_GHOST)
+    return fail(e, LJX_ERR_INVALID, "row part must be LJX_ROWS_LOCAL or LJX_ROWS_GHOST");
+  if (part == LJX_ROWS_GHOST && e->local_part_blocks < 0)
+    return fail(e, LJX_ERR_INVALID,
+                "ljx_force_rows(LJX_ROWS_GHOST) must follow ljx_force_rows(LJX_ROWS_LOCAL) after "
+                "the same ljx_density");
+  const Modes m = pass_modes(e, newton_pair);
+  ljx::Step<T> p = make_step<T>(e, a, l, scale);
+  set_pack_rules(p, e->c, m);
+  p.row_part = part == LJX_ROWS_LOCAL ? ljx::kRowsLocal : ljx::kRowsGhost;
+  e->last_scale = scale;
+  e->step_ev = true;
+  const int block0 = part == LJX_ROWS_LOCAL ? 0 : e->local_part_blocks;
+  p.partials = e->partial(kForcePart) + static_cast<long long>(block0) * ljx::kPartialWidth;
+  const int grid = launch_force<T>(e, s, p, m.force, block0, e->max_grid - block0);
+  e->local_part_blocks = part == LJX_ROWS_LOCAL ? grid : -1;
   return LJX_OK;
 }
 
@@ -1025,6 +1063,8 @@ ljx_status ljx_engine_create(const ljx_bundle *bundle, int device, ljx_engine **
         static_cast<size_t>(e->rows_cap) * e->row_cap * sizeof(int), "cudaMalloc(compacted rows)"));
     e->ccount = static_cast<int *>(device_alloc(e->rows_cap * sizeof(int), "cudaMalloc(counts)"));
     check(cudaMemset(e->ccount, 0, e->rows_cap * sizeof(int)), "cudaMemset(counts)");
+    e->ghost_rows = static_cast<unsigned char *>(device_alloc(e->rows_cap, "cudaMalloc(ghost rows)"));
+    check(cudaMemset(e->ghost_rows, 1, e->rows_cap), "cudaMemset(ghost rows)");
     e->offsets = static_cast<long long *>(
         device_alloc((static_cast<size_t>(e->rows_cap) + 1) * sizeof(long long), "cudaMalloc(offsets)"));
     check(cudaMemset(e->offsets, 0, (static_cast<size_t>(e->rows_cap) + 1) * sizeof(long long)),
@@ -1201,6 +1241,20 @@ ljx_status ljx_force(ljx_engine *e, void *stream, const ljx_atoms *atoms, const 
     auto s = static_cast<cudaStream_t>(stream);
     return e->f64 ? force_impl<double>(e, s, atoms, list, newton_pair, scale)
                   : force_impl<float>(e, s, atoms, list, newton_pair, scale);
+  });
+}
+
+ljx_status ljx_force_rows(ljx_engine *e, void *stream, const ljx_atoms *atoms,
+                          const ljx_list *list, int newton_pair, double scale, int part)
+{
+  return guarded(e, [&]() -> ljx_status {
+    const ljx_status st = check_list(e, list);
+    if (st != LJX_OK) return st;
+    if (atoms == nullptr || atoms->f == nullptr)
+      return fail(e, LJX_ERR_INVALID, "force array is missing");
+    auto s = static_cast<cudaStream_t>(stream);
+    return e->f64 ? force_rows_impl<double>(e, s, atoms, list, newton_pair, scale, part)
+                  : force_rows_impl<float>(e, s, atoms, list, newton_pair, scale, part);
   });
 }
 

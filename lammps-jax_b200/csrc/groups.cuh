@@ -271,7 +271,10 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
       }
     }
     __syncthreads();
-    if (row < p.inum && i < 0 && lane == 0) p.ccount[row] = 0;
+    if (row < p.inum && i < 0 && lane == 0) {
+      p.ccount[row] = 0;
+      p.ghost_rows[row] = 0;
+    }
     if (i >= 0) {
       widest = max(widest, listed);
       const float fix = static_cast<float>(xi.x), fiy = static_cast<float>(xi.y),
@@ -281,6 +284,7 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
       T rho = T(0);
       int kept = 0;
       int kept_twice = 0;  // owned pairs held once (kDensityHalfOwned) count for both directions
+      bool ghost = false;  // this lane kept a ghost neighbor
       if (cached) {
         // About 80 % of a row's cached candidates are kept, so each batch of 32 evaluates its
         // kept pairs in place: the idle lanes cost little (a gather costs per sector touched,
@@ -312,6 +316,7 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
           const unsigned m = __ballot_sync(kFull, keep);
           const int at = kept + __popc(m & below);
           if (keep && at < p.row_cap) crow[at] = j;
+          ghost |= keep && j >= p.nlocal;
           T r2;
           if constexpr (sizeof(T) == 8) {
             r2 = r2d;
@@ -363,6 +368,7 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
             }
           }
           const unsigned m = __ballot_sync(kFull, keep);
+          ghost |= keep && j >= p.nlocal;
           if (keep) {
             const int at = kept + __popc(m & below);
             if (at < p.row_cap) crow[at] = j;
@@ -391,12 +397,14 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
         }
       }
       rho = warp_sum(rho);
+      const bool ghost_row = __any_sync(kFull, ghost);
       if (lane == 0) {
         if (MODE == kDensityHalf || MODE == kDensityHalfOwned)
           atomicAdd(p.rho + i, rho);
         else
           p.rho[i] = rho;
         p.ccount[row] = kept;
+        p.ghost_rows[row] = ghost_row;
       }
       kept_sum += kept + kept_twice;
     }

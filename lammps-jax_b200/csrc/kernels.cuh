@@ -65,6 +65,7 @@ enum DensityMode { kDensityFull = 0, kDensityHalf = 1, kCompactOnly = 2, kDensit
 //                    pairs, forces, energy and virial as kRowsFull, from about half the pairs.
 enum ForceMode { kRowsFull = 0, kGhost = 1, kHalf = 2, kRowsHalfOwned = 3 };
 enum LjMode { kLjEdgeFull = 0, kLjEdgeHalf = 1, kLjAtomFull = 2, kLjAtomHalfPairSum = 3 };
+enum RowPart { kRowsAll = 0, kRowsLocal = 1, kRowsGhost = 2 };
 
 template <typename T> struct Vec4;
 template <> struct Vec4<float> { using type = float4; };
@@ -199,6 +200,11 @@ struct Step {
   double *eatom;
   double *vatom;
   double tally_scale;
+  // Per list row: 1 when the row keeps a ghost neighbor (written by the density passes). The
+  // force pass takes every row (kRowsAll), or only the rows without (kRowsLocal: they need no
+  // ghost F', so they can run while the F' exchange is in flight) or with one (kRowsGhost).
+  unsigned char *ghost_rows;
+  int row_part;
 };
 
 __device__ __forceinline__ double warp_sum(double v)
@@ -497,10 +503,14 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
     const int row = row0 + warp;
     const int i = s_row_i[warp];
     const int n = s_row_n[warp];
-    if (row < p.inum && i < 0 && lane == 0) p.ccount[row] = 0;
+    if (row < p.inum && i < 0 && lane == 0) {
+      p.ccount[row] = 0;
+      p.ghost_rows[row] = 0;
+    }
     if (row < p.inum && i >= 0) {
       const double4 xi = load4(p.xd4 + i);
       const float4 fi = __ldg(pos4f + i);
+      bool ghost = false;  // this lane kept a ghost neighbor
       const int si = static_cast<int>(xi.w);
       int *crow = p.cedges + static_cast<long long>(row) * p.row_cap;
       const long long rowbase = static_cast<long long>(i) * p.atom_stride;
@@ -589,6 +599,7 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
           }
         }
         const unsigned m = __ballot_sync(kFull, keep);
+        ghost |= keep && j >= p.nlocal;
         // Owned pairs held once stand for both directions in the kept-edge count.
         if (MODE == kDensityHalfOwned) kept_twice += __popc(__ballot_sync(kFull, keep && j < p.nlocal));
         if constexpr (sizeof(T) == 4) {
@@ -618,7 +629,11 @@ __global__ void LJX_DENSITY_BOUNDS k_density(const Step<T> p)
             p.rho[i] = rho;
         }
       }
-      if (lane == 0) p.ccount[row] = kept;
+      const bool ghost_row = __any_sync(kFull, ghost);
+      if (lane == 0) {
+        p.ccount[row] = kept;
+        p.ghost_rows[row] = ghost_row;
+      }
       kept_sum += kept + kept_twice;
     }
     __syncthreads();
@@ -826,6 +841,7 @@ __global__ void LJX_FORCE_BOUNDS k_force(const Step<T> p)
       n = p.ccount[row];
     }
     if (i >= p.max_atoms) continue;
+    if (p.row_part != kRowsAll && (p.ghost_rows[row] != 0) != (p.row_part == kRowsGhost)) continue;
     const V pi = load_pos(p, i);
     const int si = static_cast<int>(pi.w);
     const T fpi = FORCES ? p.fp[i] : T(0);

@@ -167,6 +167,14 @@ class Engine:
         self._check(self.lib.ljx_force(self._h, _stream(stream), ctypes.byref(atoms),
                                        ctypes.byref(nl), int(newton_pair), float(scale)))
 
+    def force_rows(self, atoms, nl, newton_pair, part, scale=1.0, stream=None):
+        """One part of the force pass (ljx_force_rows): abi.ROWS_LOCAL, the rows without a
+        ghost neighbor (they may run while the F' exchange is in flight), then abi.ROWS_GHOST,
+        the others; together they are force()."""
+        self._check(self.lib.ljx_force_rows(self._h, _stream(stream), ctypes.byref(atoms),
+                                            ctypes.byref(nl), int(newton_pair), float(scale),
+                                            int(part)))
+
     def force_only(self, atoms, nl, newton_pair, scale=1.0, stream=None):
         """The forces without the energy and virial sums (steps where LAMMPS asks for
         neither); the next read_result reports energy and virial as zero."""

@@ -296,6 +296,26 @@ class NcclHalo:
         self._check(self.lib.ljx_halo_reverse(self._h, self._s(stream), ctypes.c_void_p(rows),
                                               width, elem_bytes, 1))
 
+    def forward_under_force(self, engine, atoms, nl, newton_pair, rows, width: int,
+                            elem_bytes: int, scale: float = 1.0):
+        """The forward exchange of `rows` (F'(rho)) overlapped with the force pass: the
+        exchange runs on a side stream while the current stream runs the force pass over the
+        list rows without a ghost neighbor (ljx_force_rows, ROWS_LOCAL); the rows with one
+        (ROWS_GHOST) follow once the exchange is done. Leaves what forward() then
+        engine.force() would, with the current stream ordered after both."""
+        if not hasattr(self, "_side"):
+            self._side = torch.cuda.Stream()
+            self._ready = torch.cuda.Event()
+            self._done = torch.cuda.Event()
+        main = torch.cuda.current_stream()
+        self._ready.record(main)
+        self._side.wait_event(self._ready)
+        self.forward(rows, width, elem_bytes, stream=self._side)
+        self._done.record(self._side)
+        engine.force_rows(atoms, nl, newton_pair, abi.ROWS_LOCAL, scale)
+        main.wait_event(self._done)
+        engine.force_rows(atoms, nl, newton_pair, abi.ROWS_GHOST, scale)
+
     def reverse_forces(self, f: torch.Tensor, stream=None):
         """LAMMPS's own reverse comm of ghost force rows (newton on)."""
         self.reverse(f.data_ptr(), 3, 8, stream)

@@ -8,8 +8,11 @@ rank count) and runs one EAM step in each exchange pattern of the benchmark thro
 engine and NCCL halo (include/ljx_halo.h):
   rows-full    full list, newton off: forward F'(rho) (C3);
   half-unique  half list, newton on: reverse rho, forward F'(rho), reverse forces (C4).
-Rank 0 gathers the owned forces by global site id and compares them, and the collective energy
-and virial of ljx_read_result_all, with the CPU oracle (oracle/) on the whole periodic crystal:
+Each pattern runs twice: with the F' exchange before the force pass, and with it on a side
+stream under the force pass's rows that keep no ghost neighbor (NcclHalo.forward_under_force,
+ljx_force_rows). Rank 0 gathers the owned forces by global site id and compares them, and the
+collective energy and virial of ljx_read_result_all, with the CPU oracle (oracle/) on the whole
+periodic crystal:
 forces within 1e-10 of the largest |F|, energy and virial within 1e-12 relative. It writes a
 JSON summary and exits non-zero on a mismatch. tests/test_gpu_multirank.py launches it when a
 box has two GPUs or more.
@@ -40,7 +43,7 @@ FRACTIONS = (0.64, 0.36)
 FORCE_REL, TOTAL_REL = 1e-10, 1e-12
 
 
-def rank_step(ljx, mode, cells, rank, world, local, text, tmp):
+def rank_step(ljx, mode, cells, rank, world, local, text, tmp, overlap=False):
     from lammps_jax_b200.halo import NcclHalo, slab_swaps
     newton, half = (False, False) if mode == "rows-full" else (True, True)
     s = ljx.synth.slab_decomposition(cells, A, JITTER, SEED, rank, world, CUT, fractions=FRACTIONS)
@@ -69,9 +72,13 @@ def rank_step(ljx, mode, cells, rank, world, local, text, tmp):
         if plan.reverse_density:
             halo.reverse(rho_rows, width, elem)
         eng.embed(atoms)
-        if plan.forward_fp:
-            halo.forward(fp_rows, width, elem)
-        eng.force(atoms, nl, newton, 1.0)
+        if plan.forward_fp and overlap:
+            # The F' exchange on a side stream under the force pass's rows without ghosts.
+            halo.forward_under_force(eng, atoms, nl, newton, fp_rows, width, elem)
+        else:
+            if plan.forward_fp:
+                halo.forward(fp_rows, width, elem)
+            eng.force(atoms, nl, newton, 1.0)
         if plan.reverse_force:
             halo.reverse_forces(system.f)
         res = halo.result_all(eng)
@@ -113,8 +120,10 @@ def main():
     cells_total = (cells[0], cells[1], cells[2] * world)
     summary, ok = {"ranks": world, "cells_per_rank": cells, "modes": {}}, True
     with tempfile.TemporaryDirectory() as tmp:
-        for mode in ("rows-full", "half-unique"):
-            ids, forces, res = rank_step(ljx, mode, cells, rank, world, local, text, tmp)
+        for mode, overlap in (("rows-full", False), ("half-unique", False),
+                              ("rows-full", True), ("half-unique", True)):
+            ids, forces, res = rank_step(ljx, mode, cells, rank, world, local, text, tmp, overlap)
+            name = mode + ("+overlap" if overlap else "")
             parts = [None] * world
             dist.all_gather_object(parts, (ids, forces))
             if rank == 0:
@@ -132,7 +141,7 @@ def main():
                 good = (same_atoms and ferr <= FORCE_REL and eerr <= TOTAL_REL and
                         verr <= TOTAL_REL and res.edge_count == ref.count and not res.overflow)
                 ok &= good
-                summary["modes"][mode] = {
+                summary["modes"][name] = {
                     "atoms": int(len(g_ids)), "kept_edges": int(res.edge_count),
                     "oracle_edges": int(ref.count), "force_err_rel_max": ferr,
                     "energy": res.energy, "oracle_energy": float(ref.energy),

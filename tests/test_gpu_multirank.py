@@ -40,6 +40,6 @@ def test_two_rank_decomposition_matches_oracle(tmp_path):
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
     summary = json.loads(out.read_text())
     assert summary["pass"] and summary["ranks"] == 2
-    for mode in ("rows-full", "half-unique"):
+    for mode in ("rows-full", "half-unique", "rows-full+overlap", "half-unique+overlap"):
         m = summary["modes"][mode]
         assert m["pass"], m
