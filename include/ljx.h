@@ -206,9 +206,10 @@ ljx_status ljx_force(ljx_engine *engine, void *stream, const ljx_atoms *atoms,
 /* ljx_force in two parts, so that a rank's F'(rho) exchange overlaps its force pass (the
  * reference's forward comm of F' runs between its density and force programs, with nothing else
  * in flight: cpp/pair_jax_kokkos.cpp:523-571, cpp/pjrt/model_comm.cpp:392-472).
- * ljx_density marks each list row that keeps a ghost neighbor. LJX_ROWS_LOCAL runs the force
- * pass over the other rows, which read no ghost F' and may run while the exchange fills the ghost
- * rows of F'; LJX_ROWS_GHOST, after the exchange, runs the marked rows. The two calls, in that
+ * ljx_density marks each list row that keeps a ghost neighbor (over the candidate cache: each
+ * row with a ghost candidate, marked when the cache is built). LJX_ROWS_LOCAL runs the force
+ * pass over the unmarked rows, which read no ghost F' and may run while the exchange fills the
+ * ghost rows of F'; LJX_ROWS_GHOST, after the exchange, runs the marked rows. The two calls, in that
  * order after the same ljx_density, leave atoms->f and the step's energy and virial as one
  * ljx_force call does (sums in another order). EAM bundles only (LJ: LJX_ERR_UNSUPPORTED);
  * a ghost part without its local part fails with LJX_ERR_INVALID. */

@@ -131,6 +131,7 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
     unsigned short *slots = p.rslot + static_cast<long long>(row) * p.rcap;
     int *out = p.gatom + static_cast<long long>(g) * p.gcap;
     bool lost = false;
+    bool ghost = false;  // this lane met a ghost candidate
     int total = 0;  // distinct atoms so far (uniform over the warp)
     int got = 0;    // candidates of this lane's row so far (uniform over the row's lanes)
     const long long rowbase = static_cast<long long>(i) * p.atom_stride;
@@ -172,6 +173,7 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
       total += __popc(fm);
       __syncwarp();  // the new atoms' union indices are visible to every lane
       const unsigned cm = __ballot_sync(kFull, cand);
+      ghost |= cand && j >= p.nlocal;
       if (cand) {
         const int at = got + __popc(cm & rowlanes & below);
         if (at < p.rcap) slots[at] = uindex[h];
@@ -182,7 +184,14 @@ k_build_groups(const Step<T> p, int span, int force_build, float disp_limit, dou
     // lists instead.
     const bool spilled = __any_sync(kFull, lost || got > p.rcap) || total > kUnionMax ||
                          total > p.gcap || total > HASH * 3 / 4;
-    if (lane < kGroupRows && row < p.inum) p.rcount[row] = got;
+    // A row with a ghost among its candidates may keep a ghost pair until the next build (every
+    // kept pair is a candidate): ljx_force_rows runs it after the F' exchange. A group past
+    // capacity walks its lists, so all its rows are marked.
+    const bool row_ghost = (__ballot_sync(kFull, ghost) & rowlanes) != 0;
+    if (lane < kGroupRows && row < p.inum) {
+      p.rcount[row] = got;
+      p.ghost_rows[row] = spilled || row_ghost;
+    }
     __syncwarp();
     for (int h = lane; h < HASH / 4; h += kWarp) key4[h] = make_int4(-1, -1, -1, -1);
     __syncwarp();
@@ -271,10 +280,7 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
       }
     }
     __syncthreads();
-    if (row < p.inum && i < 0 && lane == 0) {
-      p.ccount[row] = 0;
-      p.ghost_rows[row] = 0;
-    }
+    if (row < p.inum && i < 0 && lane == 0) p.ccount[row] = 0;
     if (i >= 0) {
       widest = max(widest, listed);
       const float fix = static_cast<float>(xi.x), fiy = static_cast<float>(xi.y),
@@ -284,7 +290,6 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
       T rho = T(0);
       int kept = 0;
       int kept_twice = 0;  // owned pairs held once (kDensityHalfOwned) count for both directions
-      bool ghost = false;  // this lane kept a ghost neighbor
       if (cached) {
         // About 80 % of a row's cached candidates are kept, so each batch of 32 evaluates its
         // kept pairs in place: the idle lanes cost little (a gather costs per sector touched,
@@ -316,7 +321,6 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
           const unsigned m = __ballot_sync(kFull, keep);
           const int at = kept + __popc(m & below);
           if (keep && at < p.row_cap) crow[at] = j;
-          ghost |= keep && j >= p.nlocal;
           T r2;
           if constexpr (sizeof(T) == 8) {
             r2 = r2d;
@@ -368,7 +372,6 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
             }
           }
           const unsigned m = __ballot_sync(kFull, keep);
-          ghost |= keep && j >= p.nlocal;
           if (keep) {
             const int at = kept + __popc(m & below);
             if (at < p.row_cap) crow[at] = j;
@@ -397,14 +400,12 @@ __global__ void __launch_bounds__(kBlock, LJX_GROUP_MIN_BLOCKS) k_density_groups
         }
       }
       rho = warp_sum(rho);
-      const bool ghost_row = __any_sync(kFull, ghost);
       if (lane == 0) {
         if (MODE == kDensityHalf || MODE == kDensityHalfOwned)
           atomicAdd(p.rho + i, rho);
         else
           p.rho[i] = rho;
         p.ccount[row] = kept;
-        p.ghost_rows[row] = ghost_row;
       }
       kept_sum += kept + kept_twice;
     }

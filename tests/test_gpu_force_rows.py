@@ -1,9 +1,10 @@
 """ljx_force_rows: the EAM force pass in two parts, so that the F'(rho) exchange can run under it.
 
-ljx_density marks the list rows that keep a ghost neighbor. ROWS_LOCAL runs the force pass over
-the other rows (they read no ghost F'), ROWS_GHOST over the marked ones; in that order they must
+ljx_density marks the list rows that keep a ghost neighbor (the candidate-cache build marks rows
+with a ghost candidate). ROWS_LOCAL runs the force pass over the other rows (they read no ghost
+F'), ROWS_GHOST over the marked ones; in that order they must
 leave the forces, energy, virial and kept count of one ljx_force call, to rounding (the sums run
-in another order), in every force mode and both precisions, with the candidate cache and with
+in another order), in every force mode and both precisions, over the candidate cache and over
 the list pass. The crystal (8 x 8 x 8 fcc cells, periodic images as ghosts) has rows of both
 kinds: atoms more than rc from every face keep no ghost. The ghost part alone, out of order, and
 LJ bundles are refused. The overlap itself, with the exchange on a side stream over NCCL, is
@@ -57,9 +58,10 @@ def engine_step(pair, system, ago, split):
 def test_two_parts_equal_one_pass(tmp_path, mode, precision, cache):
     case = eam_case(elements=("Cu", "Zr"), cells=(8, 8, 8), seed=31, nr=2000, nrho=2000)
     pair, system, _ = run_pair(tmp_path, case, mode, precision)
-    ago = 0 if cache else -1
-    f_one, one, _ = engine_step(pair, system, ago, split=False)
-    f_two, two, local = engine_step(pair, system, ago, split=True)
+    # With the cache: the whole pass on the list's first step (the cache and its row marks are
+    # built), the two parts on the next step over that cache. Without: the list pass both times.
+    f_one, one, _ = engine_step(pair, system, 0 if cache else -1, split=False)
+    f_two, two, local = engine_step(pair, system, 1 if cache else -1, split=True)
     scale = float(np.max(np.abs(f_one)))
     tol = 1e-12 if precision == "float64" else 1e-5
     assert float(np.max(np.abs(f_two - f_one))) <= tol * scale
