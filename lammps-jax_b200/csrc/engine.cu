@@ -543,11 +543,11 @@ void launch_groups(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int ago
 // those of the earlier pieces, at most `cap` blocks (0: no cap).
 template <typename T, bool FORCES, bool TALLY, bool EV = true>
 int launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode,
-                    int block0 = 0, int cap = 0)
+                    int block0 = 0, int cap = 0, int waves = 1)
 {
   auto run = [&](auto kernel) {
     prefer_carveout(kernel, LJX_FORCE_CARVEOUT);
-    int grid = row_grid(e, p.inum, blocks_per_sm(kernel));
+    int grid = row_grid(e, p.inum, blocks_per_sm(kernel) * waves);
     if (cap > 0) grid = std::min(grid, cap);
     kernel<<<grid, ljx::kBlock, 0, s>>>(p);
     return grid;
@@ -571,13 +571,13 @@ int launch_force_as(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mo
 
 template <typename T, bool FORCES = true>
 int launch_force(ljx_engine *e, cudaStream_t s, const ljx::Step<T> &p, int mode, int block0 = 0,
-                 int cap = 0)
+                 int cap = 0, int waves = 1)
 {
   if (p.inum <= 0) return 0;
   // The per-atom tally variants run only when a caller asked for per-atom output.
   if (p.eatom != nullptr || p.vatom != nullptr)
-    return launch_force_as<T, FORCES, true>(e, s, p, mode, block0, cap);
-  return launch_force_as<T, FORCES, false>(e, s, p, mode, block0, cap);
+    return launch_force_as<T, FORCES, true>(e, s, p, mode, block0, cap, waves);
+  return launch_force_as<T, FORCES, false>(e, s, p, mode, block0, cap, waves);
 }
 
 template <typename T, bool FORCES, bool TALLY>
@@ -733,6 +733,9 @@ ljx_status force_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const l
 // local rows read no ghost F', so they can run while the F' exchange is in flight. The ghost
 // part writes its energy and virial partial rows after the local part's, so the step's result
 // sums both.
+#ifndef LJX_LOCAL_WAVES
+#define LJX_LOCAL_WAVES 8
+#endif
 template <typename T>
 ljx_status force_rows_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, const ljx_list *l,
                            int newton_pair, double scale, int part)
@@ -751,9 +754,15 @@ ljx_status force_rows_impl(ljx_engine *e, cudaStream_t s, const ljx_atoms *a, co
   p.row_part = part == LJX_ROWS_LOCAL ? ljx::kRowsLocal : ljx::kRowsGhost;
   e->last_scale = scale;
   e->step_ev = true;
+  // The local part runs beside the exchange's NCCL kernels, which hold some SMs' block slots
+  // when it starts. Launched as one wave of resident blocks, each walking its share of the rows,
+  // the blocks that find no slot would start only when others finish and run their whole share
+  // after them; as LJX_LOCAL_WAVES waves, a late block takes a small share. Each part writes at
+  // most half of the force partial rows.
   const int block0 = part == LJX_ROWS_LOCAL ? 0 : e->local_part_blocks;
   p.partials = e->partial(kForcePart) + static_cast<long long>(block0) * ljx::kPartialWidth;
-  const int grid = launch_force<T>(e, s, p, m.force, block0, e->max_grid - block0);
+  const int grid = launch_force<T>(e, s, p, m.force, block0, e->max_grid / 2,
+                                   part == LJX_ROWS_LOCAL ? LJX_LOCAL_WAVES : 1);
   e->local_part_blocks = part == LJX_ROWS_LOCAL ? grid : -1;
   return LJX_OK;
 }
