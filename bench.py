@@ -959,9 +959,10 @@ def main():
     ap.add_argument("--e2e-pieces", type=int, default=8,
                     help="row pieces of the e2e force pass whose force rows are copied to the "
                          "host as each finishes (ljx_force_to_host); 0: one copy after the step")
-    ap.add_argument("--fp-overlap", choices=("on", "off"), default="on",
+    ap.add_argument("--fp-overlap", choices=("on", "off"), default="off",
                     help="across GPUs, run the F' exchange under the force pass's rows without "
-                         "ghost neighbors (ljx_force_rows)")
+                         "ghost neighbors (ljx_force_rows); measured slower at 2 GPUs (force "
+                         "phase 1.85 -> 2.19 ms against a 0.04 ms exchange), so off by default")
     ap.add_argument("--quick", action="store_true",
                     help="time the device path, the e2e and the force-only legs only (no MD, "
                          "C4, float32 or CPU-baseline legs)")
