@@ -376,6 +376,26 @@ def init_ranks():
     return world, rank, local
 
 
+def algorithmic_bytes(listed, nlocal, nall, kept, precision, newton):
+    """Algorithmic bytes of one step on one rank: (density phase, force pass, whole step).
+
+    Density phase: every row's list slots read (4 B each), ilist and numneigh, each atom's
+    staged position once, the kept edges written (4 B), the kept count and rho. Force pass: the
+    row's atom and count, the kept edges read, each atom's position and F' once, f read and
+    written. Whole step: the list slots and counts, each kept edge written once and its index read
+    twice (density and force passes), and per owned atom x read by three passes (24 B each),
+    type, rho written, F' written and read, f read-modify-written (double); per ghost x three
+    times, type and F' (newton on adds the ghost's rho and f round trips)."""
+    real = 8 if precision == "float64" else 4
+    pos_bytes = 32 if precision == "float64" else 16
+    density = 4 * listed + 4 * nlocal * 2 + 32 * nall + 4 * kept + 4 * nlocal + real * nlocal
+    force = 8 * nlocal + 4 * kept + pos_bytes * nall + real * nall + 48 * nlocal
+    b_own = 3 * 24 + 4 + real + 2 * real + 48
+    b_ghost = 3 * 24 + 4 + real + ((2 * real + 48) if newton else 0)
+    step = 4 * listed + 4 * nlocal + 12 * kept + nlocal * b_own + (nall - nlocal) * b_ghost
+    return density, force, step
+
+
 def run_ljx(args):
     import tempfile
 
@@ -406,11 +426,8 @@ def run_ljx(args):
     nn = system.list.numneigh[:nlocal].to(torch.int64)
     listed = int(nn.sum().item())
     kept_local = kept_total // world
-    real = 8 if precision == "float64" else 4
-    bytes_density = (4 * listed + 4 * nlocal * 2 + 32 * nall + 4 * kept_local + 4 * nlocal +
-                     real * nlocal)
-    pos_bytes = 32 if precision == "float64" else 16
-    bytes_force = 8 * nlocal + 4 * kept_local + pos_bytes * nall + real * nall + 48 * nlocal
+    bytes_density, bytes_force, bytes_step = algorithmic_bytes(
+        listed, nlocal, nall, kept_local, precision, bool(system.newton_pair))
     # The line's roofline is the phase that moves most of the step's algorithmic bytes: the
     # density phase, which carries the list read. (By time the density and force phases are
     # about equal at C3, so a choice by time would flip between runs.) Both phases and the whole
@@ -418,15 +435,6 @@ def run_ljx(args):
     kernel = "density" if bytes_density >= bytes_force else "force"
     kbytes = bytes_density if kernel == "density" else bytes_force
     achieved = kbytes / phase[kernel] / 1e9
-    # Whole step: every row's list slots and count read, each kept edge written once and its
-    # index read twice (density and force passes), and per owned atom x read by three passes
-    # (24 B each), type, rho written, F' written and read, f read-modify-written (double); per
-    # ghost x three times, type and F' (newton on adds the ghost's rho and f round trips).
-    newton = bool(system.newton_pair)
-    b_own = 3 * 24 + 4 + real + 2 * real + 48
-    b_ghost = 3 * 24 + 4 + real + ((2 * real + 48) if newton else 0)
-    bytes_step = (4 * listed + 4 * nlocal + 12 * kept_local + nlocal * b_own +
-                  (nall - nlocal) * b_ghost)
     peak, peak_kind = peaks()
     # The engine caches candidates only for lists that live at least 4 steps (kCacheMinPeriod in
     # csrc/engine.cu); shorter-lived lists take the list pass.
